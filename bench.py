@@ -1,0 +1,395 @@
+"""Benchmark of the quantized DiT/LLM inner loop on B200 (one JSON line on rank 0).
+
+Workloads:
+  gemm    C1  W8A8 rotated linear 1024x3072x3072 (block-128 Hadamard), TOPS
+  attn    C2  fused attention B2 H24 S4056 d128, fp16 QK (and attn_i8: int8 QK), TFLOPS
+  w4a8    C3  W4A8 linear 2809x3072x8192, group 128, TOPS
+  dit     C4  8 DiT blocks, B2 (CFG) x 3321 tokens, hidden 3072, 24 heads, MLP 8192, ms/step (default)
+  decode  C5  single-token decode, 36 layers, hidden 2560, 32/8 heads, MLP 9728, ctx 1024, ms/token
+
+``--impl reference`` times the reference's CPU path (the oracle restatement, on all host threads) for the same
+workload and metric. Run with torchrun for N > 1 GPUs (one process per GPU).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl != "reference":
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1 and dist.is_initialized():
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world > 1 and dist.is_initialized():
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+    return x
+
+
+def timed(run_step, steps, warmup, world, kernel_events=None):
+    """W warm-up steps, then K steps between a barrier + synchronize on both sides; CUDA events on the current
+    stream. Returns (total ms over the K steps, max over ranks)."""
+    for i in range(warmup):
+        run_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        run_step(warmup + i)
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return max_over_ranks(start.elapsed_time(end), world)
+
+
+def kernel_ms(events):
+    """Average duration of the dominant kernel from (start, end) event pairs recorded around its launches."""
+    torch.cuda.synchronize()
+    times = [s.elapsed_time(e) for s, e in events]
+    return sum(times) / len(times) if times else None
+
+
+def pkg():
+    import __graft_entry__
+
+    return __graft_entry__.load_package()
+
+
+# ---------------------------------------------------------------------------------------------------------- workloads
+class GemmC1:
+    name = "gemm"
+    metric = "W8A8 GEMM TOPS (C1: 1024x3072x3072 rotated linear, pre-pass + GEMM)"
+    unit = "TOPS"
+    higher = True
+    M, K, N = 1024, 3072, 3072
+
+    def __init__(self, dev):
+        from oracle import weights as ow
+
+        p = pkg()
+        self.ops, self.int8_gemm = p.ops, p.int8_gemm
+        g = np.random.default_rng(0)
+        x = g.standard_normal((self.M, self.K)).astype(np.float32)
+        x[:, g.choice(self.K, self.K // 100, replace=False)] *= 20
+        self.x_host = torch.from_numpy(x.astype(np.float16)).pin_memory()
+        w = (g.standard_normal((self.N, self.K)) * 0.02).astype(np.float32)
+        wq, ws = ow.quantize_per_channel(ow.sylvester_rotate(w))
+        bias = (g.standard_normal(self.N) * 0.01).astype(np.float16)
+        # Rotating sets of inputs and weights, together larger than 2x L2, so each step reads from DRAM.
+        per = self.M * self.K * 3 + self.N * self.K + self.M * self.N * 2
+        self.sets = max(2, math.ceil(2 * L2_BYTES / per))
+        self.xs = [self.x_host.to(dev) for _ in range(self.sets)]
+        self.ws = [torch.from_numpy(wq).to(dev) for _ in range(self.sets)]
+        self.wscale = torch.from_numpy(ws).to(dev)
+        self.bias = torch.from_numpy(bias).to(dev)
+        self.qs = [(torch.empty((self.M, self.K), dtype=torch.int8, device=dev),
+                    torch.empty((self.M,), dtype=torch.float32, device=dev)) for _ in range(self.sets)]
+        self.outs = [torch.empty((self.M, self.N), dtype=torch.float16, device=dev) for _ in range(self.sets)]
+        self.y_host = torch.empty((self.M, self.N), dtype=torch.float16).pin_memory()
+        self.events = []
+        self.launches_per_step = 2
+        self.ops_per_step = 2.0 * self.M * self.N * self.K
+
+    def step(self, i, record=False):
+        s = i % self.sets
+        q = self.ops.quant_pack_a(self.xs[s], 128, out=self.qs[s])
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.ops.gemm(q[0], q[1], self.ws[s], self.wscale, self.bias, out=self.outs[s])
+        if record:
+            e1.record()
+            self.events.append((e0, e1))
+
+    def e2e_step(self, i):
+        s = i % self.sets
+        x = self.x_host.to(self.xs[s].device, non_blocking=True)
+        y = self.int8_gemm.linear(x, self.ws[s], self.wscale, self.bias, rotate=True, rot_group=128)
+        self.y_host.copy_(y, non_blocking=True)
+
+    h2d_bytes = property(lambda self: self.M * self.K * 2)
+    d2h_bytes = property(lambda self: self.M * self.N * 2)
+
+    def value(self, ms, steps, world):
+        return self.ops_per_step * steps * world / (ms * 1e-3) / 1e12
+
+    def roofline(self, peaks, kms):
+        peak = 2.0 * peaks["bf16_tflops"]
+        achieved = self.ops_per_step / (kms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS", "frac": achieved / peak,
+                "traffic": None, "kernel": "gemm_w8a8_kernel",
+                "note": f"int8 peak = 2 x {peaks['source']} bf16 ({peaks['bf16_tflops']} TFLOP/s)"}
+
+    config = {"workload": "C1 W8A8 rotated linear", "M": 1024, "K": 3072, "N": 3072, "rotation": "block-128 Sylvester",
+              "l2": "rotating input/weight sets > 2x L2"}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        from oracle import gemm as ogemm
+        from oracle import quant as oq
+        from oracle import weights as ow
+
+        torch.set_num_threads(threads)
+        g = np.random.default_rng(0)
+        M, K, N = GemmC1.M, GemmC1.K, GemmC1.N
+        x = g.standard_normal((M, K)).astype(np.float16)
+        wq, ws = ow.quantize_per_channel(ow.sylvester_rotate((g.standard_normal((N, K)) * 0.02).astype(np.float32)))
+        bias = (g.standard_normal(N) * 0.01).astype(np.float16)
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < 10:
+            q, s, _ = oq.prepass(x, 128)
+            ogemm.epilogue(ogemm.int_mm(q, wq), s, ws, bias)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        return 2.0 * M * N * K / dt / 1e12, f"{reps} full C1 linears (oracle pre-pass + torch._int_mm + epilogue)"
+
+
+class AttnC2:
+    name = "attn"
+    unit = "TFLOPS"
+    higher = True
+    B, H, S = 2, 24, 4056
+
+    def __init__(self, dev, int8_qk=False):
+        p = pkg()
+        self.ops, self.attention = p.ops, p.attention
+        self.int8_qk = int8_qk
+        self.metric = f"attention TFLOPS (C2: B2 H24 S4056 d128, {'int8' if int8_qk else 'fp16'} QK)"
+        gen = torch.Generator().manual_seed(2)
+        shape = (self.B, self.H, self.S, 128)
+        self.host = [torch.randn(shape, generator=gen).half().pin_memory() for _ in range(3)]
+        per = 4 * self.B * self.H * self.S * 128 * 2
+        self.sets = max(2, math.ceil(2 * L2_BYTES / per))
+        self.qkv = [[t.to(dev) for t in self.host] for _ in range(self.sets)]
+        self.outs = [torch.empty(shape, dtype=torch.float16, device=dev) for _ in range(self.sets)]
+        lib = p._lib.load()
+        n = lib.b2_attention_workspace_bytes(self.B, self.H, self.H, self.S, self.S, int(int8_qk))
+        self.ws = torch.empty(max(n, 16), dtype=torch.uint8, device=dev)
+        self.out_host = torch.empty(shape, dtype=torch.float16).pin_memory()
+        self.events = []
+        self.launches_per_step = 3 if int8_qk else 1
+        self.flops = 4.0 * self.B * self.H * self.S * self.S * 128
+        self.config = {"workload": "C2 fused attention", "B": 2, "H": 24, "S": 4056, "d": 128,
+                       "qk": "int8" if int8_qk else "fp16", "l2": "rotating q/k/v sets > 2x L2"}
+
+    def step(self, i, record=False):
+        s = i % self.sets
+        q, k, v = self.qkv[s]
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.ops.attention(q, k, v, self.outs[s], 128 ** -0.5, int8_qk=self.int8_qk, workspace=self.ws)
+        if record:
+            e1.record()
+            self.events.append((e0, e1))
+
+    def e2e_step(self, i):
+        dev = self.qkv[0][0].device
+        q, k, v = (t.to(dev, non_blocking=True) for t in self.host)
+        out = self.attention.attention_hip(q, k, v, self.H, skip_reshape=True, skip_output_reshape=True,
+                                           int8_qk=self.int8_qk)
+        self.out_host.copy_(out, non_blocking=True)
+
+    h2d_bytes = property(lambda self: 3 * self.B * self.H * self.S * 128 * 2)
+    d2h_bytes = property(lambda self: self.B * self.H * self.S * 128 * 2)
+
+    def value(self, ms, steps, world):
+        return self.flops * steps * world / (ms * 1e-3) / 1e12
+
+    def roofline(self, peaks, kms):
+        peak = peaks["bf16_tflops"]
+        achieved = self.flops / (kms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": None, "kernel": "attention_kernel",
+                "note": f"fp16 peak = {peaks['source']} bf16 dense" + ("; includes the int8 Q/K quantization" if self.int8_qk else "")}
+
+    @staticmethod
+    def cpu_baseline(threads, int8_qk=False):
+        from oracle import attention as oatt
+
+        torch.set_num_threads(threads)
+        B, H, S = AttnC2.B, AttnC2.H, AttnC2.S
+        gen = torch.Generator().manual_seed(2)
+        q, k, v = (torch.randn((1, 1, S, 128), generator=gen).half() for _ in range(3))
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < 10:
+            oatt.attention_bmm(q, k, v)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        flops = 4.0 * S * S * 128
+        return flops / dt / 1e12, f"{reps} single (batch, head) slices of C2 through the reference's attention_bmm (fp16 CPU), scaled per slice"
+
+
+WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True)}
+
+
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    name = args.workload
+    if name == "gemm":
+        v, sample = GemmC1.cpu_baseline(threads)
+        metric, unit, higher, cfg = GemmC1.metric, GemmC1.unit, True, GemmC1.config
+    elif name in ("attn", "attn_i8"):
+        v, sample = AttnC2.cpu_baseline(threads, name == "attn_i8")
+        w = AttnC2.__new__(AttnC2)
+        metric = f"attention TFLOPS (C2: B2 H24 S4056 d128, {'int8' if name == 'attn_i8' else 'fp16'} QK)"
+        unit, higher = "TFLOPS", True
+        cfg = {"workload": "C2 fused attention", "B": 2, "H": 24, "S": 4056, "d": 128}
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": f"no CPU reference arm for workload {name}"}))
+        return
+    line = {"metric": metric, "value": v, "unit": unit, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": higher, "impl": "reference", "dtype": "int8/fp16", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}, "vs_baseline": None}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="gemm", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks = load_peaks()
+    wl = WORKLOADS[args.workload](dev)
+
+    # Kernel timing pass (dominant kernel), then the timed whole-job pass, then the end-to-end pass.
+    for i in range(args.warmup):
+        wl.step(i)
+    wl.events = []
+    for i in range(args.steps):
+        wl.step(i, record=True)
+    kms = kernel_ms(wl.events)
+
+    with Clocks(local) as clocks:
+        ms = timed(wl.step, args.steps, args.warmup, world)
+    e2e_ms = timed(wl.e2e_step, args.steps, args.warmup, world)
+
+    line = {"metric": wl.metric, "value": wl.value(ms, args.steps, world), "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": wl.higher, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp16",
+            "data": "synthetic (seeded, BASELINE shapes)", "config": dict(wl.config, parallelism=f"replicas x{world}"),
+            "e2e": {"value": wl.value(e2e_ms, args.steps, world), "unit": wl.unit,
+                    "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
+            "roofline": wl.roofline(peaks, kms), "kernel_ms": kms, "clocks": clocks.summary(),
+            "gpu_launches": wl.launches_per_step * args.steps}
+    if rank == 0 and not args.no_cpu_baseline:
+        v, sample = type(wl).cpu_baseline(os.cpu_count() or 1) if hasattr(type(wl), "cpu_baseline") else (None, "")
+        line["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1 and dist.is_initialized():
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,544 @@
+// Fused attention for head dim 128 on sm_100a, fp16 QK or int8 QK, fp16 PV, fp32 softmax.
+//
+// Semantics follow hip_attention.hip:
+//   fp16 (attn, :280-373): s = q.k (fp32 accumulate); log2-domain online softmax with c = scale*log2(e);
+//     rows of a 32-row warp rescale together, and only when some row's block max exceeds m + 8 (:333-340);
+//     p = exp2(s*c - m) rounded to fp16 for PV, l sums the fp32 p (:343-347); out = fp16(o * (1/l)).
+//   int8 QK (pack_kv_i8 :56-103, attn_i8 :160-278): per-row q and per-key k scales max(|x|max/127, 1e-30),
+//     values rint(x/scale) (half-even); s = ((float)int_dot * (qs*c)) * ks; p = exp2(s - m); PV stays fp16.
+// Keys past Lk are masked (score -inf), queries past Lq are not stored.
+//
+// One CTA computes a 128-row Q tile of one (batch, head):
+//   warp 0      TMA: Q once, then K/V tiles of 128 keys into a 2-deep ring (fp16: two 64-column boxes each)
+//   warp 1      TMEM owner and single-thread tcgen05.mma issuer:
+//                 S[j%2] = Q K_j^T   (TMEM, 128 columns each, double-buffered so QK_{j+1} overlaps softmax_j)
+//                 O     += P_j V_j   (TMEM, 128 fp32 columns; V is the MN-major B operand in its natural layout)
+//   warps 2..5  softmax: thread = query row = TMEM lane; reads S, rescales O in TMEM when needed,
+//               writes P (fp16) to shared memory in the 128-byte-swizzled K-major layout, final O / l.
+#include "common.cuh"
+#include "host.hpp"
+
+namespace b2 {
+namespace {
+
+__device__ unsigned int g_status;
+
+constexpr int TQ = 128;   // query rows per CTA
+constexpr int TK = 128;   // keys per tile
+constexpr int HD = 128;   // head dim
+constexpr int ATT_THREADS = 192;
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <bool I8>
+struct AttCfg {
+    static constexpr int Q_BYTES = I8 ? TQ * HD : TQ * HD * 2;
+    static constexpr int K_BYTES = I8 ? TK * HD : TK * HD * 2;
+    static constexpr int V_BYTES = TK * HD * 2;
+    static constexpr int P_BYTES = TQ * TK * 2;
+    static constexpr int KS_BYTES = I8 ? TK * 4 : 0;
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+    static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+    static constexpr int OFF_KS = OFF_P + P_BYTES;
+    static constexpr int OFF_BAR = OFF_KS + 2 * KS_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+};
+
+struct AttArgs {
+    __half* out;
+    int64_t sob, soh, sol;
+    const float* qscale;  // int8: [B*H, Lq]
+    int Lq, Lk, H, rep;
+    float scale_log2;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void ld32(uint32_t taddr, uint32_t* r) {
+    tmem_ld32_wait(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+}
+
+template <bool I8>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKS, const AttArgs a) {
+    using C_ = AttCfg<I8>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::OFF_BAR);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* v_full = bars + 3;   // [2]
+    uint64_t* k_empty = bars + 5;  // [2]
+    uint64_t* v_empty = bars + 7;  // [2]
+    uint64_t* s_full = bars + 9;   // [2]
+    uint64_t* s_free = bars + 11;  // [2]
+    uint64_t* p_full = bars + 13;
+    uint64_t* o_done = bars + 14;
+    uint64_t* drain = bars + 15;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * TQ;
+    const int bh = blockIdx.y;
+    const int b = bh / a.H, h = bh % a.H;
+    const int hkv = h / a.rep;
+    const int bkv = b * (a.H / a.rep) + hkv;
+    const int n_tiles = (a.Lk + TK - 1) / TK;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&v_full[i], 1);
+            // int8: the key scales in the K stage are read by the softmax threads too.
+            mbar_init(&k_empty[i], I8 ? 1 + 128 : 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 128);
+        }
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        if (I8) tma_prefetch_desc(&tmKS);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    unsigned char* sQ = smem + C_::OFF_Q;
+    unsigned char* sK = smem + C_::OFF_K;
+    unsigned char* sV = smem + C_::OFF_V;
+    unsigned char* sP = smem + C_::OFF_P;
+    float* sKS = reinterpret_cast<float*>(smem + C_::OFF_KS);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t k_issued = 0, v_issued = 0, k_ph = 0, v_ph = 0;
+            bool ok = true;
+            mbar_arrive_expect_tx(q_full, C_::Q_BYTES);
+            if (I8) {
+                tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
+            } else {
+                tma_load_4d(sQ, &tmQ, q_full, 0, q0, h, b);
+                tma_load_4d(sQ + TQ * 128, &tmQ, q_full, 64, q0, h, b);
+            }
+            auto load_k = [&](int j) -> bool {
+                const int st = j & 1;
+                if (!mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, &g_status, B2_DEV_TIMEOUT_PRODUCER)) return false;
+                mbar_arrive_expect_tx(&k_full[st], C_::K_BYTES + C_::KS_BYTES);
+                unsigned char* dst = sK + st * C_::K_BYTES;
+                if (I8) {
+                    tma_load_3d(dst, &tmK, &k_full[st], 0, j * TK, bkv);
+                    tma_load_2d(sKS + st * TK, &tmKS, &k_full[st], j * TK, bkv);
+                } else {
+                    tma_load_4d(dst, &tmK, &k_full[st], 0, j * TK, hkv, b);
+                    tma_load_4d(dst + TK * 128, &tmK, &k_full[st], 64, j * TK, hkv, b);
+                }
+                k_issued |= 1u << st;
+                k_ph = (k_ph & ~(1u << st)) | (((j >> 1) & 1u) << st);
+                return true;
+            };
+            auto load_v = [&](int j) -> bool {
+                const int st = j & 1;
+                if (!mbar_wait(&v_empty[st], ((j >> 1) & 1) ^ 1, abort_flag, &g_status, B2_DEV_TIMEOUT_PRODUCER)) return false;
+                mbar_arrive_expect_tx(&v_full[st], C_::V_BYTES);
+                unsigned char* dst = sV + st * C_::V_BYTES;
+                tma_load_4d(dst, &tmV, &v_full[st], 0, j * TK, hkv, b);
+                tma_load_4d(dst + TK * 128, &tmV, &v_full[st], 64, j * TK, hkv, b);
+                v_issued |= 1u << st;
+                v_ph = (v_ph & ~(1u << st)) | (((j >> 1) & 1u) << st);
+                return true;
+            };
+            ok = load_k(0);
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                if (j + 1 < n_tiles && !load_k(j + 1)) ok = false;
+                if (ok && !load_v(j)) ok = false;
+            }
+            if (!ok) {
+                mbar_wait_drain(q_full, 0, 100000000ull);
+                for (int s = 0; s < 2; ++s) {
+                    if ((k_issued >> s) & 1)
+                        if (!mbar_wait_drain(&k_full[s], (k_ph >> s) & 1, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+                    if ((v_issued >> s) & 1)
+                        if (!mbar_wait_drain(&v_full[s], (v_ph >> s) & 1, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = I8 ? idesc_make(2, 1, 0, 0, TQ, TK) : idesc_make(1, 0, 0, 0, TQ, TK);
+            constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 1, TQ, HD);
+            bool ok = mbar_wait(q_full, 0, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA);
+            const uint32_t q_addr = smem_u32(sQ);
+            const uint32_t p_addr = smem_u32(sP);
+            for (int j = 0; j <= n_tiles && ok; ++j) {
+                if (j < n_tiles) {
+                    const int st = j & 1, sb = j & 1;
+                    if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
+                    if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(sK + st * C_::K_BYTES);
+                    const uint32_t d = tmem + sb * TK;
+                    if (I8) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_i8_ss(d, sdesc_sw128(q_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 32, 16, 1024),
+                                      idesc_qk, kk != 0);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint32_t off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
+                            mma_f16_ss(d, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
+                                       idesc_qk, kk != 0);
+                        }
+                    }
+                    tc_commit(&k_empty[st]);
+                    tc_commit(&s_full[sb]);
+                }
+                if (j >= 1) {
+                    const int jj = j - 1, st = jj & 1;
+                    if (!mbar_wait(p_full, jj & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
+                    if (!mbar_wait(&v_full[st], (jj >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_u32(sV + st * C_::V_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t a_off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
+                        mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + a_off, 16, 1024),
+                                   sdesc_sw128(v_addr + kk * 2048, TK * 128, 1024), idesc_pv, (jj | kk) != 0);
+                    }
+                    tc_commit(&v_empty[st]);
+                    tc_commit(o_done);
+                }
+            }
+            tc_commit(drain);
+            if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+        }
+    } else {
+        // Softmax warpgroup: thread -> query row r, TMEM lane r.
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        const uint32_t tO = tmem + lane_base + 256;
+        float m = -1e30f, l = 0.f;
+        float qs_c = 0.f;
+        if (I8) {
+            const int qr = min(q0 + r, a.Lq - 1);
+            qs_c = __fmul_rn(a.qscale[(int64_t)bh * a.Lq + qr], a.scale_log2);
+        }
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int sb = j & 1;
+            if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ld32(tmem + lane_base + sb * TK + c * 32, sr + c * 32);
+            tc_fence_before();
+            mbar_arrive(&s_free[sb]);
+
+            const int valid = a.Lk - j * TK;  // keys of this tile that exist
+            float* x = reinterpret_cast<float*>(sr);  // scores, converted in place
+            float mx = -1e30f;
+            if (I8) {
+                const float* ks = sKS + (j & 1) * TK;
+#pragma unroll
+                for (int i = 0; i < 128; ++i) {
+                    const float v = __fmul_rn(__fmul_rn((float)(int32_t)sr[i], qs_c), ks[i]);
+                    x[i] = i < valid ? v : -1e30f;
+                    mx = fmaxf(mx, x[i]);
+                }
+                // Key scales of this stage are consumed.
+                mbar_arrive(&k_empty[j & 1]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 128; ++i) {
+                    x[i] = i < valid ? __uint_as_float(sr[i]) : -1e30f;
+                    mx = fmaxf(mx, x[i]);
+                }
+                mx *= a.scale_log2;
+            }
+            bool o_ready = false;
+            if (__any_sync(0xffffffffu, mx > m + 8.f)) {
+                const float mn = fmaxf(m, mx);
+                const float alpha = ex2(m - mn);
+                m = mn;
+                l *= alpha;
+                if (j > 0) {
+                    if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                        ok = false;
+                        break;
+                    }
+                    o_ready = true;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32_wait(tO + c * 32, o);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(tO + c * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // p = exp2(s*c - m), fp16 for PV; l sums the fp32 values.
+            uint32_t ph[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                float p0, p1;
+                if (I8) {
+                    p0 = ex2(x[2 * i] - m);
+                    p1 = ex2(x[2 * i + 1] - m);
+                } else {
+                    p0 = ex2(fmaf(x[2 * i], a.scale_log2, -m));
+                    p1 = ex2(fmaf(x[2 * i + 1], a.scale_log2, -m));
+                }
+                l += p0 + p1;
+                const __half2 hp = __floats2half2_rn(p0, p1);
+                ph[i] = *reinterpret_cast<const uint32_t*>(&hp);
+            }
+            if (j > 0 && !o_ready) {
+                // P of the previous tile is still being read by its PV MMA.
+                if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                    ok = false;
+                    break;
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                unsigned char* atom = sP + (c >> 3) * (TQ * 128);
+                const int chunk = (c & 7) ^ (r & 7);
+                *reinterpret_cast<uint4*>(atom + r * 128 + chunk * 16) =
+                    make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            const bool row_ok = q0 + r < a.Lq;
+            __half* dst = a.out + (int64_t)b * a.sob + (int64_t)h * a.soh + (int64_t)(q0 + r) * a.sol;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tmem_ld32_wait(tO + c * 32, o);
+                if (row_ok) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        uint4 u;
+                        __half2* hu = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+                        for (int z = 0; z < 4; ++z)
+                            hu[z] = __floats2half2_rn(__uint_as_float(o[8 * e + 2 * z]) * inv,
+                                                      __uint_as_float(o[8 * e + 2 * z + 1]) * inv);
+                        *reinterpret_cast<uint4*>(dst + c * 32 + 8 * e) = u;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// Per-row int8 quantization of Q or K rows of 128 values (hip_attention.hip:67-93, :172-194):
+// scale = max(absmax / 127, 1e-30), q = rint(x / scale). 16 threads per row, 8 values each.
+__global__ void __launch_bounds__(256) quant_rows_i8_kernel(const __half* __restrict__ x, int64_t sb, int64_t sh,
+                                                           int64_t sl, int H, int L, int rows, int8_t* __restrict__ q,
+                                                           float* __restrict__ scale, int64_t scale_ld) {
+    const int n = blockIdx.x * 16 + (threadIdx.x >> 4);
+    const int t = threadIdx.x & 15;
+    const bool valid = n < rows;
+    const int nn = valid ? n : rows - 1;
+    const int l = nn % L, bh = nn / L, h = bh % H, b = bh / H;
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + b * sb + h * sh + (int64_t)l * sl) + t);
+    const __half2* hv = reinterpret_cast<const __half2*>(&raw);
+    float f[8];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 v = __half22float2(hv[i]);
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+        mx = fmaxf(mx, fmaxf(fabsf(v.x), fabsf(v.y)));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o, 16));
+    const float s = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
+    if (!valid) return;
+    uint32_t w[2];
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int v = (int)fminf(fmaxf(rintf(__fdiv_rn(f[4 * d + i], s)), -128.f), 127.f);
+            acc |= (uint32_t)(v & 255) << (8 * i);
+        }
+        w[d] = acc;
+    }
+    *reinterpret_cast<uint2*>(q + (int64_t)n * HD + t * 8) = make_uint2(w[0], w[1]);
+    if (t == 0) scale[(int64_t)bh * scale_ld + l] = s;
+}
+
+struct Views {
+    const void* p;
+    int64_t sb, sh, sl;
+};
+
+inline int64_t rup(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+struct I8Layout {
+    int64_t q_off, k_off, qs_off, ks_off, total, ks_ld;
+};
+
+I8Layout i8_layout(int B, int H, int Hkv, int Lq, int Lk) {
+    I8Layout o;
+    o.ks_ld = rup(Lk, 4);
+    o.q_off = 0;
+    o.k_off = rup(o.q_off + (int64_t)B * H * Lq * HD, 1024);
+    o.qs_off = rup(o.k_off + (int64_t)B * Hkv * Lk * HD, 1024);
+    o.ks_off = rup(o.qs_off + (int64_t)B * H * Lq * 4, 1024);
+    o.total = rup(o.ks_off + (int64_t)B * Hkv * o.ks_ld * 4, 1024);
+    return o;
+}
+
+int map_heads(CUtensorMap* m, const Views& v, int B, int H, int L) {
+    const uint64_t dims[4] = {(uint64_t)HD, (uint64_t)L, (uint64_t)H, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)v.sl * 2, (uint64_t)v.sh * 2, (uint64_t)v.sb * 2};
+    const uint32_t box[4] = {64, 128, 1, 1};
+    return make_map_4d(m, v.p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dims, strides, box);
+}
+
+int map_rows_i8(CUtensorMap* m, const void* base, int64_t rows_per_head, int heads) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(B2_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t d3[3] = {(cuuint64_t)HD, (cuuint64_t)rows_per_head, (cuuint64_t)heads};
+    cuuint64_t s3[2] = {(cuuint64_t)HD, (cuuint64_t)rows_per_head * HD};
+    cuuint32_t b3[3] = {128, 128, 1};
+    cuuint32_t e3[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), d3, s3, b3, e3,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled(3d int8) failed with %d", (int)r);
+    return B2_OK;
+}
+
+template <bool I8>
+int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tks,
+                     const AttArgs& a, int B, cudaStream_t s) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (int rc = set_smem(attention_kernel<I8>, AttCfg<I8>::SMEM)) return rc;
+        configured[dev] = true;
+    }
+    dim3 grid((a.Lq + TQ - 1) / TQ, B * a.H);
+    attention_kernel<I8><<<grid, ATT_THREADS, AttCfg<I8>::SMEM, s>>>(tq, tk, tv, tks, a);
+    return check_launch("attention_kernel");
+}
+
+}  // namespace
+
+unsigned int read_status_attention() {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+    if (v) cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    return v;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" int64_t b2_attention_workspace_bytes(int B, int H, int Hkv, int Lq, int Lk, int int8_qk) {
+    if (!int8_qk) return 0;
+    if (B <= 0 || H <= 0 || Hkv <= 0 || Lq <= 0 || Lk <= 0) return 0;
+    return i8_layout(B, H, Hkv, Lq, Lk).total;
+}
+
+extern "C" int b2_attention(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k, int64_t skb,
+                            int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl,
+                            uint16_t* out, int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk,
+                            float scale, int int8_qk, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!q || !k || !v || !out) return fail(B2_ERR_INVALID, "attention: null pointer");
+    if (B < 0 || H <= 0 || Hkv <= 0 || Lq < 0 || Lk <= 0 || H % Hkv)
+        return fail(B2_ERR_INVALID, "attention: bad shape B=%d H=%d Hkv=%d Lq=%d Lk=%d", B, H, Hkv, Lq, Lk);
+    if (!aligned16(out) || (sob * 2) % 16 || (soh * 2) % 16 || (sol * 2) % 16)
+        return fail(B2_ERR_UNSUPPORTED, "attention: out must be 16-byte aligned with 16-byte strides");
+    if (B == 0 || Lq == 0) return B2_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    AttArgs a{};
+    a.out = reinterpret_cast<__half*>(out);
+    a.sob = sob;
+    a.soh = soh;
+    a.sol = sol;
+    a.Lq = Lq;
+    a.Lk = Lk;
+    a.H = H;
+    a.rep = H / Hkv;
+    a.scale_log2 = scale * LOG2E;
+    CUtensorMap tq, tk, tv, tks;
+    const Views vq{q, sqb, sqh, sql}, vk{k, skb, skh, skl}, vv{v, svb, svh, svl};
+    if (int rc = map_heads(&tv, vv, B, Hkv, Lk)) return rc;
+    if (!int8_qk) {
+        if (int rc = map_heads(&tq, vq, B, H, Lq)) return rc;
+        if (int rc = map_heads(&tk, vk, B, Hkv, Lk)) return rc;
+        tks = tk;
+        return launch_attention<false>(tq, tk, tv, tks, a, B, s);
+    }
+    const I8Layout lay = i8_layout(B, H, Hkv, Lq, Lk);
+    if (!workspace || workspace_bytes < lay.total)
+        return fail(B2_ERR_INVALID, "attention: int8 QK needs %lld bytes of workspace", (long long)lay.total);
+    if (!aligned16(workspace)) return fail(B2_ERR_UNSUPPORTED, "attention: workspace must be 16-byte aligned");
+    if (!aligned16(q) || !aligned16(k) || (sqb | sqh | sql | skb | skh | skl) % 8)
+        return fail(B2_ERR_UNSUPPORTED, "attention: q and k must be 16-byte aligned with 16-byte strides");
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    int8_t* q8 = reinterpret_cast<int8_t*>(ws + lay.q_off);
+    int8_t* k8 = reinterpret_cast<int8_t*>(ws + lay.k_off);
+    float* qs = reinterpret_cast<float*>(ws + lay.qs_off);
+    float* ks = reinterpret_cast<float*>(ws + lay.ks_off);
+    const int qrows = B * H * Lq, krows = B * Hkv * Lk;
+    quant_rows_i8_kernel<<<(qrows + 15) / 16, 256, 0, s>>>(reinterpret_cast<const __half*>(q), sqb, sqh, sql, H, Lq, qrows,
+                                                          q8, qs, Lq);
+    if (int rc = check_launch("quant_rows_i8_kernel(q)")) return rc;
+    quant_rows_i8_kernel<<<(krows + 15) / 16, 256, 0, s>>>(reinterpret_cast<const __half*>(k), skb, skh, skl, Hkv, Lk,
+                                                          krows, k8, ks, lay.ks_ld);
+    if (int rc = check_launch("quant_rows_i8_kernel(k)")) return rc;
+    if (int rc = map_rows_i8(&tq, q8, Lq, B * H)) return rc;
+    if (int rc = map_rows_i8(&tk, k8, Lk, B * Hkv)) return rc;
+    if (int rc = make_map_2d(&tks, ks, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Lk, (uint64_t)B * Hkv, lay.ks_ld * 4, TK, 1,
+                             CU_TENSOR_MAP_SWIZZLE_NONE))
+        return rc;
+    a.qscale = qs;
+    return launch_attention<true>(tq, tk, tv, tks, a, B, s);
+}

@@ -1,0 +1,280 @@
+// Single-token decode kernels: fp32 Hadamard rotation, int8 GEMV, split-KV fp32 decode attention.
+//
+// Semantics follow int8_gemv.hip:
+//   rotate      : radix-4 regular-Hadamard stages, stride x4, y[i] = sum - 2 x[3-i], then * rsqrt(group) (:108-129)
+//   gemv_i8     : out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32                         (:131-162)
+//   attn_decode : q * scale, online softmax with expf over a split of ceil(len/32) positions, merge (:198-271)
+//
+// The GEMV streams the int8 weight once from HBM with 16-byte non-allocating loads, several rows and
+// several steps in flight per warp. int8 -> fp32 goes through a byte permute into the mantissa of
+// 2^23 (exact), which keeps the conversion off the narrow conversion pipe.
+#include "common.cuh"
+#include "host.hpp"
+
+namespace b2 {
+namespace {
+
+constexpr int DEC_SPLITS = 32;
+constexpr int HEAD = 128;
+
+// ---------------------------------------------------------------- rotate
+__global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, float* __restrict__ out, int group) {
+    extern __shared__ float s[];
+    const float* in = x + (int64_t)blockIdx.x * group;
+    for (int i = threadIdx.x; i < group; i += 256) s[i] = in[i];
+    __syncthreads();
+    for (int stride = 1; stride < group; stride *= 4) {
+        for (int q = threadIdx.x; q < group / 4; q += 256) {
+            const int i = (q / stride) * stride * 4 + q % stride;
+            const float a = s[i], b = s[i + stride], c = s[i + 2 * stride], d = s[i + 3 * stride];
+            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
+            s[i] = __fsub_rn(sum, __fmul_rn(2.f, d));
+            s[i + stride] = __fsub_rn(sum, __fmul_rn(2.f, c));
+            s[i + 2 * stride] = __fsub_rn(sum, __fmul_rn(2.f, b));
+            s[i + 3 * stride] = __fsub_rn(sum, __fmul_rn(2.f, a));
+        }
+        __syncthreads();
+    }
+    // group is a power of 4, so the normalisation is an exact power of two.
+    const float norm = __fdiv_rn(1.f, sqrtf((float)group));
+    float* o = out + (int64_t)blockIdx.x * group;
+    for (int i = threadIdx.x; i < group; i += 256) o[i] = __fmul_rn(s[i], norm);
+}
+
+// ---------------------------------------------------------------- gemv_i8
+__device__ __forceinline__ float i8f(uint32_t w_biased, int i) {
+    // bytes of w_biased are b + 128; 0x4B0000uu is 2^23 + u exactly.
+    return __int_as_float(__byte_perm(w_biased, 0x4B000000u, 0x7540u | i)) - 8388736.f;
+}
+
+__device__ __forceinline__ float dot16(const uint4 w, const float4 (&x)[4], float acc) {
+    const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        acc = fmaf(i8f(wv[j], 0), x[j].x, acc);
+        acc = fmaf(i8f(wv[j], 1), x[j].y, acc);
+        acc = fmaf(i8f(wv[j], 2), x[j].z, acc);
+        acc = fmaf(i8f(wv[j], 3), x[j].w, acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_ROWS = 2;     // rows per warp
+constexpr int GEMV_UNROLL = 4;   // 512-value steps in flight per row
+
+// x is staged in shared memory in reading order: step s, sub-chunk j, lane l -> float4 index (s*4+j)*32+l,
+// so each float4 read of a warp is conflict-free. K % 16 == 0; a partial last step is masked.
+__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_i8_kernel(const float* __restrict__ x, const int8_t* __restrict__ w,
+                                                                 const float* __restrict__ scale,
+                                                                 const float* __restrict__ bias, float* __restrict__ out,
+                                                                 int N, int K) {
+    extern __shared__ float4 xs[];
+    const int steps = (K + 511) / 512;
+    for (int i = threadIdx.x; i < steps * 128; i += blockDim.x) {
+        const int s = i >> 7, r = i & 127, l = r >> 2, j = r & 3;
+        const int k = i * 4;
+        xs[(s * 4 + j) * 32 + l] = k < K ? *reinterpret_cast<const float4*>(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS;
+    if (row0 >= N) return;
+    float acc[GEMV_ROWS] = {};
+    const int8_t* wr[GEMV_ROWS];
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r) wr[r] = w + (int64_t)min(row0 + r, N - 1) * K + lane * 16;
+    const bool full_steps = (K % 512) == 0;
+    int s = 0;
+    for (; s + GEMV_UNROLL <= steps && (full_steps || s + GEMV_UNROLL < steps); s += GEMV_UNROLL) {
+        uint4 v[GEMV_UNROLL][GEMV_ROWS];
+#pragma unroll
+        for (int u = 0; u < GEMV_UNROLL; ++u)
+#pragma unroll
+            for (int r = 0; r < GEMV_ROWS; ++r) v[u][r] = ld_stream(wr[r] + (s + u) * 512);
+#pragma unroll
+        for (int u = 0; u < GEMV_UNROLL; ++u) {
+            float4 xv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) xv[j] = xs[((s + u) * 4 + j) * 32 + lane];
+#pragma unroll
+            for (int r = 0; r < GEMV_ROWS; ++r) acc[r] = dot16(v[u][r], xv, acc[r]);
+        }
+    }
+    for (; s < steps; ++s) {
+        if (s * 512 + lane * 16 >= K) break;
+        float4 xv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[j] = xs[(s * 4 + j) * 32 + lane];
+#pragma unroll
+        for (int r = 0; r < GEMV_ROWS; ++r) acc[r] = dot16(ld_stream(wr[r] + s * 512), xv, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r) {
+        float v = acc[r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const int n = row0 + r;
+        if (lane == 0 && n < N) {
+            const float y = v * scale[n];
+            out[n] = bias ? y + bias[n] : y;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- decode attention
+constexpr int DEC_WARPS = 8;
+
+template <int GROUP>
+__global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                                    const float* __restrict__ v,
+                                                                    const int32_t* __restrict__ lengths,
+                                                                    float* __restrict__ partial, float* __restrict__ stats,
+                                                                    int capacity, int kv_heads, float scale) {
+    __shared__ float4 acc_s[DEC_WARPS][GROUP][HEAD / 4];
+    __shared__ float max_s[DEC_WARPS][GROUP], sum_s[DEC_WARPS][GROUP];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.y / kv_heads, kvh = blockIdx.y % kv_heads, split = blockIdx.x;
+    const int length = min(lengths[b], capacity);
+    const int chunk = (length + DEC_SPLITS - 1) / DEC_SPLITS;
+    const int end = min((split + 1) * chunk, length);
+    const int first_head = (b * kv_heads + kvh) * GROUP;
+
+    float4 qv[GROUP], acc[GROUP];
+    float mx[GROUP], sum[GROUP];
+#pragma unroll
+    for (int g = 0; g < GROUP; ++g) {
+        const float4 t = reinterpret_cast<const float4*>(q + (int64_t)(first_head + g) * HEAD)[lane];
+        qv[g] = make_float4(t.x * scale, t.y * scale, t.z * scale, t.w * scale);
+        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        mx[g] = -1e30f;
+        sum[g] = 0.f;
+    }
+    for (int j = split * chunk + warp; j < end; j += DEC_WARPS) {
+        const int64_t row = ((int64_t)(b * capacity + j) * kv_heads + kvh) * HEAD;
+        const float4 kv = __ldg(reinterpret_cast<const float4*>(k + row) + lane);
+        const float4 vv = __ldg(reinterpret_cast<const float4*>(v + row) + lane);
+#pragma unroll
+        for (int g = 0; g < GROUP; ++g) {
+            float d = qv[g].x * kv.x + qv[g].y * kv.y + qv[g].z * kv.z + qv[g].w * kv.w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            const float next = fmaxf(mx[g], d);
+            const float keep = expf(mx[g] - next), p = expf(d - next);
+            sum[g] = sum[g] * keep + p;
+            acc[g].x = acc[g].x * keep + vv.x * p;
+            acc[g].y = acc[g].y * keep + vv.y * p;
+            acc[g].z = acc[g].z * keep + vv.z * p;
+            acc[g].w = acc[g].w * keep + vv.w * p;
+            mx[g] = next;
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < GROUP; ++g) {
+        acc_s[warp][g][lane] = acc[g];
+        if (lane == 0) {
+            max_s[warp][g] = mx[g];
+            sum_s[warp][g] = sum[g];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < GROUP * HEAD; i += DEC_WARPS * 32) {
+        const int g = i / HEAD, d = i % HEAD;
+        float top = max_s[0][g];
+#pragma unroll
+        for (int w = 1; w < DEC_WARPS; ++w) top = fmaxf(top, max_s[w][g]);
+        float value = 0.f, total = 0.f;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; ++w) {
+            const float keep = expf(max_s[w][g] - top);
+            value += reinterpret_cast<const float*>(&acc_s[w][g][0])[d] * keep;
+            total += sum_s[w][g] * keep;
+        }
+        const int64_t at = (int64_t)(first_head + g) * DEC_SPLITS + split;
+        partial[at * HEAD + d] = value;
+        if (d == 0) {
+            stats[at * 2] = top;
+            stats[at * 2 + 1] = total;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(HEAD) attn_merge_kernel(const float* __restrict__ partial, const float* __restrict__ stats,
+                                                         float* __restrict__ out) {
+    const int64_t head = blockIdx.x;
+    const float* st = stats + head * DEC_SPLITS * 2;
+    float top = st[0];
+    for (int s = 1; s < DEC_SPLITS; ++s) top = fmaxf(top, st[s * 2]);
+    float value = 0.f, total = 0.f;
+    for (int s = 0; s < DEC_SPLITS; ++s) {
+        const float keep = expf(st[s * 2] - top);
+        value += partial[(head * DEC_SPLITS + s) * HEAD + threadIdx.x] * keep;
+        total += st[s * 2 + 1] * keep;
+    }
+    out[head * HEAD + threadIdx.x] = value / total;
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_rotate(const float* x, float* out, int64_t n, int group, void* stream) {
+    if (!x || !out || n < 0) return fail(B2_ERR_INVALID, "rotate: bad arguments");
+    if (group < 4 || group > 16384 || (group & (group - 1)) || (__builtin_ctz(group) & 1))
+        return fail(B2_ERR_UNSUPPORTED, "rotate: group %d must be a power of 4 in [4, 16384]", group);
+    if (n % group) return fail(B2_ERR_UNSUPPORTED, "rotate: %lld values is not a multiple of group %d", (long long)n, group);
+    if (n == 0) return B2_OK;
+    const int smem = group * 4;
+    if (smem > 48 * 1024)
+        if (int rc = set_smem(rotate_kernel, smem)) return rc;
+    rotate_kernel<<<(unsigned)(n / group), 256, smem, (cudaStream_t)stream>>>(x, out, group);
+    return check_launch("rotate_kernel");
+}
+
+extern "C" int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
+                          void* stream) {
+    if (!x || !w || !scale || !out || N < 0 || K <= 0) return fail(B2_ERR_INVALID, "gemv_i8: bad arguments");
+    if (K % 16) return fail(B2_ERR_UNSUPPORTED, "gemv_i8: K=%d must be a multiple of 16", K);
+    if (!aligned16(x) || !aligned16(w)) return fail(B2_ERR_UNSUPPORTED, "gemv_i8: x and w must be 16-byte aligned");
+    if (N == 0) return B2_OK;
+    const int steps = (K + 511) / 512;
+    const int smem = steps * 512 * 4;
+    if (smem > 200 * 1024) return fail(B2_ERR_UNSUPPORTED, "gemv_i8: K=%d too large", K);
+    if (smem > 48 * 1024)
+        if (int rc = set_smem(gemv_i8_kernel, smem)) return rc;
+    const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
+    gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(x, w, scale, bias,
+                                                                                                       out, N, K);
+    return check_launch("gemv_i8_kernel");
+}
+
+extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out,
+                              float* partial, float* stats, int batch, int heads, int kv_heads, int capacity, float scale,
+                              void* stream) {
+    if (!q || !k || !v || !lengths || !out || !partial || !stats) return fail(B2_ERR_INVALID, "attn_decode: null pointer");
+    if (batch < 0 || heads <= 0 || kv_heads <= 0 || capacity <= 0 || heads % kv_heads)
+        return fail(B2_ERR_INVALID, "attn_decode: bad shape");
+    const int group = heads / kv_heads;
+    if (batch == 0) return B2_OK;
+    dim3 grid(DEC_SPLITS, batch * kv_heads);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (group) {
+        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 8: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        default: return fail(B2_ERR_UNSUPPORTED, "attn_decode: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
+    }
+    if (int rc = check_launch("attn_decode_kernel")) return rc;
+    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
+    return check_launch("attn_merge_kernel");
+}

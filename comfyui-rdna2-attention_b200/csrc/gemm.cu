@@ -1,0 +1,330 @@
+// W8A8 GEMM for sm_100a: C[M,N] = epilogue(A[M,K] int8 . B[N,K]^T int8), int32 accumulation in TMEM.
+//
+// Replaces int8_gemm.hip gemm_body (:315-406) and pack_b (:271-276). The weight is read as stored
+// (int8 [N, K], K-major) by TMA, so there is no per-call re-layout. Epilogue semantics (:371-405):
+//   y = (float)acc * as[m] * ws[n] (+ (float)bias[n]) -> fp16
+//   residual: out = fp16(R[m,n] + fp16(G[m / L, n] * y))
+//
+// Structure: a persistent kernel, one CTA per SM, 6 warps.
+//   warp 0      TMA producer: 128x128 A tiles and BNx128 B tiles (128-byte swizzle) into a STAGES-deep ring
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=BN, K=32 per instruction)
+//   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (each warp its 32-lane quarter), dequant,
+//               bias, residual, fp16 stores
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the main loop of tile i+1.
+#include "common.cuh"
+#include "host.hpp"
+
+namespace b2 {
+namespace {
+
+__device__ unsigned int g_status;
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // bytes = int8 values per k-block (one 128-byte swizzle atom)
+constexpr int GEMM_THREADS = 192;
+
+template <int BN>
+struct Cfg {
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK;
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+};
+
+struct GemmArgs {
+    const float* as;
+    const float* ws;
+    const __half* bias;
+    __half* C;
+    int32_t* C32;
+    const __half* R;
+    const __half* G;
+    int L;
+    int M, N, K;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+    using C_ = Cfg<BN>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::STAGES * C_::STAGE_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + C_::STAGES;
+    uint64_t* tfull = bars + 2 * C_::STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_m = (g.M + BM - 1) / BM, num_n = (g.N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int KB = (g.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C_::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C_::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t keep = l2_policy_evict_last();
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;  // bit s: stage s has a load in flight that nobody consumed yet (for draining)
+            uint32_t issued_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, &g_status, B2_DEV_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* sa = smem + stage * C_::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+                    tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+                    tma_load_2d_hint(sa + C_::A_BYTES, &tmB, &full[stage], kb * BK, n0, keep);
+                    issued |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == C_::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let every copy this thread started land before the CTA leaves.
+                for (int s = 0; s < C_::STAGES; ++s)
+                    if (issued & (1u << s))
+                        if (!mbar_wait_drain(&full[s], (issued_phase >> s) & 1, 100000000ull))
+                            atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_make(2, 1, 0, 0, BM, BN);  // S32 <- INT8 x INT8, both K-major
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+                const int acc = it & 1;
+                const uint32_t acc_phase = (it >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * C_::STAGE_BYTES);
+                    const uint64_t a_desc = sdesc_sw128(a_addr, 16, 1024);
+                    const uint64_t b_desc = sdesc_sw128(a_addr + C_::A_BYTES, 16, 1024);
+#pragma unroll
+                    for (int k = 0; k < BK / 32; ++k)
+                        mma_i8_ss(d_tmem, a_desc + (uint64_t)(k * 2), b_desc + (uint64_t)(k * 2), idesc,
+                                  (kb | k) != 0);
+                    tc_commit(&empty[stage]);
+                    if (++stage == C_::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+            }
+            // Every MMA issued above completes before TMEM is released.
+            tc_commit(drain);
+            if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int row_local = quarter * 32 + lane;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+            const int acc = it & 1;
+            const uint32_t acc_phase = (it >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
+            tc_fence_after();
+            const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+            const int m = m0 + row_local;
+            const bool row_ok = m < g.M;
+            const float sa = (row_ok && g.as) ? g.as[m] : 0.f;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32_wait(taddr + c * 32, r);
+                const int nb = n0 + c * 32;
+                if (!row_ok || nb >= g.N) continue;
+                if (g.C32) {
+                    int32_t* dst = g.C32 + (int64_t)m * g.N + nb;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (nb + 4 * j < g.N)
+                            *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+                    continue;
+                }
+                __half* dst = g.C + (int64_t)m * g.N + nb;
+                const __half* res = g.R ? g.R + (int64_t)m * g.N + nb : nullptr;
+                const __half* gate = g.R ? g.G + (int64_t)(m / g.L) * g.N + nb : nullptr;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (nb + 8 * j >= g.N) break;
+                    const float4 w0 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j));
+                    const float4 w1 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j) + 1);
+                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    if (g.bias) {
+                        const uint4 braw = __ldg(reinterpret_cast<const uint4*>(g.bias + nb + 8 * j));
+                        const __half2* bh = reinterpret_cast<const __half2*>(&braw);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __half22float2(bh[e]);
+                            bv[2 * e] = f.x;
+                            bv[2 * e + 1] = f.y;
+                        }
+                    }
+                    float y[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = __fmul_rn(__fmul_rn((float)(int32_t)r[8 * j + e], sa), wv[e]);
+                        y[e] = round_h(g.bias ? __fadd_rn(v, bv[e]) : v);
+                    }
+                    if (res) {
+                        const uint4 rraw = *reinterpret_cast<const uint4*>(res + 8 * j);
+                        const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gate + 8 * j));
+                        const __half2* rh = reinterpret_cast<const __half2*>(&rraw);
+                        const __half2* gh = reinterpret_cast<const __half2*>(&graw);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 rf = __half22float2(rh[e]), gf = __half22float2(gh[e]);
+                            y[2 * e] = round_h(__fadd_rn(rf.x, round_h(__fmul_rn(gf.x, y[2 * e]))));
+                            y[2 * e + 1] = round_h(__fadd_rn(rf.y, round_h(__fmul_rn(gf.y, y[2 * e + 1]))));
+                        }
+                    }
+                    uint4 o;
+                    __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
+                    *reinterpret_cast<uint4*>(dst + 8 * j) = o;
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, C_::TMEM_COLS);
+}
+
+template <int BN>
+int launch_bn(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_t stream) {
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.M, g.K, BK, BM)) return rc;
+    if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.K, BK, BN)) return rc;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (int rc = set_smem(gemm_w8a8_kernel<BN>, Cfg<BN>::SMEM)) return rc;
+        configured[dev] = true;
+    }
+    const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    gemm_w8a8_kernel<BN><<<grid, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, g);
+    return check_launch("gemm_w8a8_kernel");
+}
+
+int run(const int8_t* A, const int8_t* B, GemmArgs& g, cudaStream_t stream) {
+    if (!A || !B) return fail(B2_ERR_INVALID, "gemm: null operand");
+    if (g.M < 0 || g.N <= 0 || g.K <= 0) return fail(B2_ERR_INVALID, "gemm: bad shape M=%d N=%d K=%d", g.M, g.N, g.K);
+    if (g.K % 16) return fail(B2_ERR_UNSUPPORTED, "gemm: K=%d must be a multiple of 16", g.K);
+    if (g.N % 8) return fail(B2_ERR_UNSUPPORTED, "gemm: N=%d must be a multiple of 8", g.N);
+    if (!aligned16(A) || !aligned16(B)) return fail(B2_ERR_UNSUPPORTED, "gemm: A and B must be 16-byte aligned");
+    if (g.M == 0) return B2_OK;
+    // Wide tiles when they fill the machine; half-width tiles when the grid would be too sparse.
+    const int tiles256 = ((g.M + BM - 1) / BM) * ((g.N + 255) / 256);
+    if (tiles256 >= sm_count()) return launch_bn<256>(A, B, g, stream);
+    return launch_bn<128>(A, B, g, stream);
+}
+
+}  // namespace
+
+unsigned int read_status_gemm() {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+    if (v) cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    return v;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const float* ws, const uint16_t* bias,
+                       uint16_t* C, int M, int N, int K, const uint16_t* R, const uint16_t* G, int L, void* stream) {
+    if (!as || !ws || !C) return fail(B2_ERR_INVALID, "gemm: null scale or output");
+    if (R && (!G || L <= 0)) return fail(B2_ERR_INVALID, "gemm: residual needs a gate and L > 0");
+    if (!aligned16(C) || !aligned16(ws) || (bias && !aligned16(bias)) || (R && (!aligned16(R) || !aligned16(G))))
+        return fail(B2_ERR_UNSUPPORTED, "gemm: C, ws, bias, R, G must be 16-byte aligned");
+    GemmArgs g{};
+    g.as = as;
+    g.ws = ws;
+    g.bias = reinterpret_cast<const __half*>(bias);
+    g.C = reinterpret_cast<__half*>(C);
+    g.R = reinterpret_cast<const __half*>(R);
+    g.G = reinterpret_cast<const __half*>(G);
+    g.L = L > 0 ? L : 1;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    return run(A, B, g, (cudaStream_t)stream);
+}
+
+extern "C" int b2_gemm_i32(const int8_t* A, const int8_t* B, int32_t* C32, int M, int N, int K, void* stream) {
+    if (!C32) return fail(B2_ERR_INVALID, "gemm_i32: null output");
+    if (!aligned16(C32)) return fail(B2_ERR_UNSUPPORTED, "gemm_i32: output must be 16-byte aligned");
+    GemmArgs g{};
+    g.C32 = C32;
+    g.L = 1;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    return run(A, B, g, (cudaStream_t)stream);
+}

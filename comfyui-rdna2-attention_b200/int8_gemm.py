@@ -1,0 +1,243 @@
+"""W8A8 linear layers, the drop-in for the reference's int8_gemm.py.
+
+It keeps the reference's entry points and its hand-off protocol with the Int8 loader (ComfyUI-INT8-Fast-ROCM):
+``wrap`` returns the ``int8_linear`` that replaces the pack's ``triton_int8_linear(_per_row)`` (int8_gemm.py:105-129),
+``rotate_activation`` leaves the ConvRot rotation to the pre-pass kernel by parking the tensor in ``pending``
+(:132-142), ``swiglu_forward`` hands the up projection to the down layer's quantization (:160-167),
+``quantize_block_input`` / ``block_forward`` fuse a Krea-2 block (:176-226), ``enable`` installs the patches (:247-271).
+Module globals are the same side channels as the reference's (:25-41).
+
+Differences, all by design of this build: every linear runs the sm_100a kernels (pre-pass + tcgen05 GEMM reading the
+weight as stored: no pack_b), for any row count, so MIN_ROWS is 1; inputs the kernels cannot take raise instead of
+falling back to the pack's Triton path; the rotation group is a parameter (256 = ConvRot as in the reference, 128 =
+the block-128 configuration).
+"""
+import functools
+import logging
+import sys
+
+import torch
+import torch.nn.functional as F
+
+from . import hip_attention, ops, rms_norm
+
+MIN_ROWS = 1
+MAX_ROT_K = 16384
+ROT_GROUP = 256
+
+originals = {}
+fusable = False
+pending = None
+situ_next = False
+swiglu_up = None
+sigmoid_gate = None
+shared = None
+residual = None
+swiglu_fusable = False
+
+
+def quantized(M, K, device):
+    """(int8 [M, K], fp32 [M]) activation buffers (int8_gemm.py:51-53; plain row-major here)."""
+    return (torch.empty((M, K), dtype=torch.int8, device=device), torch.empty((M,), dtype=torch.float32, device=device))
+
+
+def run(x, weight, weight_scale, bias, rotate=False, up=None, gate=None, activations=None, res=None, rot_group=ROT_GROUP):
+    """Pre-pass (unless ``activations`` are given) then GEMM. x (M, K) fp16; weight (N, K) int8; weight_scale (N,)
+    fp32; res = (R (M, N) fp16, G (M / L, N) fp16) adds R + G * y. Returns (M, N) fp16 (int8_gemm.py:56-80)."""
+    M = x.shape[0] if activations is None else activations[0].shape[0]
+    N, K = weight.shape
+    group = rot_group if rotate else 0
+    if activations is None:
+        out = quantized(M, K, x.device)
+        if up is not None:
+            activations = ops.swiglu_quant_pack_a(x, up, group, out=out)
+        elif gate is not None:
+            activations = ops.gate_quant_pack_a(x, gate, group, out=out)
+        else:
+            activations = ops.quant_pack_a(x, group, out=out)
+    a_q, a_s = activations
+    R, G, L = (None, None, 1)
+    if res is not None:
+        R = res[0].reshape(M, N).contiguous()
+        G = res[1].reshape(-1, N).contiguous()
+        L = M // G.shape[0]
+    return ops.gemm(a_q, a_s, weight, weight_scale, bias, residual=R, gate=G, L=L)
+
+
+def linear(x, weight, weight_scale, bias, rotate=False, situ=False, up=None, gate=None, activations=None, res=None,
+           rot_group=ROT_GROUP):
+    """x is (M, K) fp16, weight (N, K) int8 and weight_scale (N,) fp32. With up, x is the gate of a SwiGLU. With gate,
+    x is multiplied by its sigmoid. Returns (M, N) fp16 (int8_gemm.py:83-87)."""
+    if situ:
+        raise NotImplementedError("the situ (Anima) activation is not part of this build's pre-pass")
+    return run(x, weight, weight_scale, bias, rotate, up, gate, activations, res, rot_group)
+
+
+def ineligible(x, weight, bias, compute_dtype, x_q):
+    N, K = weight.shape
+    if x_q is not None:
+        return "pre-quantized x_q"
+    if x.dtype != torch.float16 or compute_dtype != torch.float16:
+        return "non-fp16 input or compute dtype"
+    if bias is not None and bias.dtype != torch.float16:
+        return "non-fp16 bias"
+    if N % 8 or K % 16:
+        return f"N={N} must be a multiple of 8 and K={K} of 16"
+    return None
+
+
+def wrap(original):
+    def int8_linear(x, weight, weight_scale, bias=None, compute_dtype=torch.float16, x_q=None):
+        global pending, situ_next, swiglu_up, sigmoid_gate, residual
+        rotate, situ, up, gate, res = x is pending, situ_next, swiglu_up, sigmoid_gate, residual
+        pending, situ_next, swiglu_up, sigmoid_gate, residual = None, False, None, None, None
+        N, K = weight.shape
+        reason = ineligible(x, weight, bias, compute_dtype, x_q)
+        if reason:
+            raise NotImplementedError(f"int8_linear: {reason}")
+        if isinstance(weight_scale, torch.Tensor) and weight_scale.numel() == N:
+            scale = weight_scale.reshape(N).float().contiguous()
+        else:
+            scale = torch.full((N,), float(weight_scale), dtype=torch.float32, device=x.device)
+        out = linear(x.reshape(-1, x.shape[-1]).contiguous(), weight.contiguous(), scale, bias, rotate, situ,
+                     None if up is None else up.reshape(-1, K).contiguous(), gate, shared, res)
+        return out.reshape(x.shape[:-1] + (N,))
+    return int8_linear
+
+
+def wrap_w4a4(original):
+    """The reference runs the Int4 loader's W4A4 layers on gemm_i4 (int8_gemm.py:90-103). This build's int4 path is
+    W4A8 with group-128 scales (int4_gemm.py); per-channel W4A4 layers are not taken over."""
+    def convrot_w4a4_forward(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation=False,
+                             qweight_unpacked=None, x_rot=None, orig_shape=None):
+        raise NotImplementedError("per-channel W4A4 layers are not supported by this build (W4A8 group-128 only)")
+    return convrot_w4a4_forward
+
+
+def rotate_activation(x, H, group_size):
+    """ConvRot hand-off (int8_gemm.py:132-142): the next int8_linear rotates inside its pre-pass."""
+    global pending
+    if shared is not None:
+        return x
+    if situ_next or swiglu_up is not None or sigmoid_gate is not None:
+        pending = x
+        return x
+    if fusable and group_size == ROT_GROUP and x.dtype == torch.float16 and x.dim() == 2 and x.shape[1] % ROT_GROUP == 0 \
+            and x.shape[1] <= MAX_ROT_K:
+        pending = x
+        return x
+    return originals["rotate_activation"](x, H, group_size)
+
+
+def fuse_act(layer, x, K):
+    """Layers whose activation, ConvRot and quantization run as one pre-pass (int8_gemm.py:145-150)."""
+    return (getattr(layer, "_is_quantized", False) and getattr(layer, "_use_convrot", False) and not getattr(layer, "_is_w4a8", False)
+            and getattr(layer, "_convrot_groupsize", 0) == ROT_GROUP and not getattr(layer, "lora_patches", None)
+            and x.dtype == torch.float16 and K == layer.in_features and layer.in_features % ROT_GROUP == 0
+            and layer.in_features <= MAX_ROT_K)
+
+
+def swiglu_forward(module, x):
+    """SwiGLU with the activation folded into the down layer's quantization (int8_gemm.py:160-167)."""
+    global swiglu_up
+    gate, up = module.gate(x), module.up(x)
+    if swiglu_fusable and isinstance(module.down, originals["layer"]) and fuse_act(module.down, gate, gate.shape[-1]):
+        swiglu_up = up
+        return module.down(gate)
+    return module.down(F.silu(gate).mul_(up))
+
+
+def patch_swiglu(model):
+    for name, module in model.get_model_object("diffusion_model").named_modules():
+        if type(module).__name__ == "SwiGLU":
+            model.add_object_patch(f"diffusion_model.{name}.forward", functools.partial(swiglu_forward, module))
+
+
+def quantize_block_input(x, norm, scale, shift, rot_group=ROT_GROUP):
+    """Sets ``shared`` to the quantized (1 + scale) * norm(x) + shift that all of a block's input linears read
+    (int8_gemm.py:176-186)."""
+    global shared
+    B, L, K = x.shape
+    weight = norm.scale.to(dtype=torch.float32, device=x.device).contiguous()
+    s = (1 + scale).to(torch.float16).reshape(-1, K).contiguous()
+    t = shift.to(torch.float16).reshape(-1, K).contiguous()
+    shared = ops.mod_quant_pack_a(x.reshape(B * L, K), weight, s, t, L, norm.eps, rot_group)
+
+
+def block_forward(module, int8_qk, x, vec, freqs, mask=None, timestep_zero_index=None, transformer_options={}):
+    """Krea-2 SingleStreamBlock.forward with everything between the matmuls fused (int8_gemm.py:189-226)."""
+    global shared, swiglu_up, sigmoid_gate, residual
+    attn, mlp = module.attn, module.mlp
+    patches = transformer_options.get("patches", {})
+    if (mask is not None or timestep_zero_index is not None or freqs is None or "attn1_patch" in patches
+            or "attn1_output_patch" in patches or x.dtype != torch.float16 or attn.headdim != rms_norm.HEAD_DIM):
+        raise NotImplementedError("block_forward: masks, patches, non-fp16 or head dim != 128 are not supported")
+    B, L, D = x.shape
+    prescale, preshift, pregate, postscale, postshift, postgate = module.mod(vec)
+    try:
+        quantize_block_input(x, module.prenorm, prescale, preshift)
+        q, k, v, gate = attn.wq(x), attn.wk(x), attn.wv(x), attn.gate(x)
+        shared = None
+
+        q = rms_norm.rms_norm_rope(q, attn.heads, attn.qknorm.qnorm, freqs)
+        k = rms_norm.rms_norm_rope(k, attn.kvheads, attn.qknorm.knorm, freqs)
+        v = v.view(B, L, attn.kvheads, attn.headdim).transpose(1, 2)
+        out = torch.empty((B, L, attn.heads, attn.headdim), dtype=x.dtype, device=x.device)
+        hip_attention.attention(q, k, v, out.transpose(1, 2), attn.headdim ** -0.5, int8_qk)
+
+        sigmoid_gate = gate.view(-1, D)
+        residual = x, pregate.contiguous()
+        x = attn.wo(out.view(B, L, D))
+
+        quantize_block_input(x, module.postnorm, postscale, postshift)
+        gate, up = mlp.gate(x), mlp.up(x)
+        shared = None
+
+        swiglu_up = up
+        residual = x, postgate.contiguous()
+        return mlp.down(gate)
+    finally:
+        shared = swiglu_up = sigmoid_gate = residual = None
+
+
+def patch_block(model, int8_qk):
+    for name, module in model.get_model_object("diffusion_model").named_modules():
+        if type(module).__name__ == "SingleStreamBlock":
+            model.add_object_patch(f"diffusion_model.{name}.forward", functools.partial(block_forward, module, int8_qk))
+
+
+def wrap_forward(forward):
+    def int8_forward(self, x):
+        global fusable
+        fusable = not getattr(self, "lora_patches", None)
+        try:
+            return forward(self, x)
+        finally:
+            fusable = False
+    return int8_forward
+
+
+def enable(on):
+    """Installs (or removes) the patches in the loaded Int8/Int4 packs (int8_gemm.py:247-271)."""
+    global swiglu_fusable
+    pack = next((m for name, m in sys.modules.items() if name.endswith(".int8_quant") and hasattr(m, "triton_int8_linear_per_row")), None)
+    int4 = next((m for name, m in sys.modules.items() if name.endswith(".int4_quant") and hasattr(m, "convrot_w4a4_forward")), None)
+    if int4 is not None:
+        originals.setdefault("convrot_w4a4_forward", int4.convrot_w4a4_forward)
+        int4.convrot_w4a4_forward = wrap_w4a4(originals["convrot_w4a4_forward"]) if on else originals["convrot_w4a4_forward"]
+    if pack is None:
+        if on:
+            logging.warning("rdna2_b200: int8_gemm skipped, ComfyUI-INT8-Fast-ROCM is not loaded.")
+        return
+    convrot = next(m for name, m in sys.modules.items() if name.endswith(".convrot") and hasattr(m, "rotate_activation"))
+    layer = pack.Int8TensorwiseOps.Linear
+    if "forward" not in originals:
+        originals.update(layer=layer, triton_int8_linear=pack.triton_int8_linear,
+                         triton_int8_linear_per_row=pack.triton_int8_linear_per_row,
+                         rotate_activation=convrot.rotate_activation, build_hadamard=convrot.build_hadamard,
+                         forward=layer.forward)
+    for name in ("triton_int8_linear", "triton_int8_linear_per_row"):
+        setattr(pack, name, wrap(originals[name]) if on else originals[name])
+    convrot.rotate_activation = rotate_activation if on else originals["rotate_activation"]
+    layer.forward = wrap_forward(originals["forward"]) if on else originals["forward"]
+    swiglu_fusable = on and getattr(pack, "_TRITON_AVAILABLE", True)

@@ -1,0 +1,197 @@
+"""Tensor-level wrappers of the C-ABI: shape/dtype checks, output allocation by the caller side (as the
+reference allocates with torch.empty, e.g. int8_gemm.py:51-53,60), launch on torch's current stream."""
+import math
+
+import torch
+
+from . import _lib
+from ._lib import F, I, I64, call, ptr, require_cuda, stream
+
+ROT_NONE, ROT_BLOCK128, ROT_CONVROT = 0, 128, 256
+
+
+def _half2d(x, name):
+    if x.dtype != torch.float16 or x.dim() != 2 or x.stride(-1) != 1:
+        raise RuntimeError(f"{name} must be a 2D fp16 tensor with a contiguous last dimension")
+
+
+def quant_pack_a(x, rot_group=ROT_NONE, out=None):
+    """Per-row int8 of fp16 rows x [M, K] after an optional rotation. Returns (int8 [M, K], fp32 [M])."""
+    require_cuda(x)
+    _half2d(x, "x")
+    M, K = x.shape
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=x.device),
+                                        torch.empty((M,), dtype=torch.float32, device=x.device))
+    call("b2_quant_pack_a", ptr(x), I64(x.stride(0)), ptr(q), ptr(s), I(M), I(K), I(rot_group), stream())
+    return q, s
+
+
+def quant_pack_a_segments(x, K, rot_group, seg, seg_stride, M, ldx, out=None):
+    """Rows gathered from segments: element k of row m sits at x[m*ldx + (k//seg)*seg_stride + k%seg]."""
+    require_cuda(x)
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=x.device),
+                                        torch.empty((M,), dtype=torch.float32, device=x.device))
+    call("b2_quant_pack_a_seg", ptr(x), I64(ldx), I(seg), I64(seg_stride), ptr(q), ptr(s), I(M), I(K), I(rot_group),
+         stream())
+    return q, s
+
+
+def swiglu_quant_pack_a(gate, up, rot_group=ROT_NONE, act_out=None, out=None):
+    """int8 of fp16(fp16(silu(gate)) * up) after an optional rotation. gate, up fp16 [M, K] with equal strides."""
+    require_cuda(gate, up)
+    _half2d(gate, "gate")
+    _half2d(up, "up")
+    if gate.shape != up.shape or gate.stride(0) != up.stride(0):
+        raise RuntimeError("gate and up must have the same shape and row stride")
+    M, K = gate.shape
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=gate.device),
+                                        torch.empty((M,), dtype=torch.float32, device=gate.device))
+    call("b2_swiglu_quant_pack_a", ptr(gate), ptr(up), I64(gate.stride(0)), ptr(q), ptr(s), I(M), I(K), I(rot_group),
+         ptr(act_out), stream())
+    return q, s
+
+
+def gate_quant_pack_a(x, gate, rot_group=ROT_NONE, act_out=None, out=None):
+    """int8 of fp16(x * fp16(sigmoid(gate))) after an optional rotation."""
+    require_cuda(x, gate)
+    _half2d(x, "x")
+    _half2d(gate, "gate")
+    if x.shape != gate.shape or x.stride(0) != gate.stride(0):
+        raise RuntimeError("x and gate must have the same shape and row stride")
+    M, K = x.shape
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=x.device),
+                                        torch.empty((M,), dtype=torch.float32, device=x.device))
+    call("b2_gate_quant_pack_a", ptr(x), ptr(gate), I64(x.stride(0)), ptr(q), ptr(s), I(M), I(K), I(rot_group),
+         ptr(act_out), stream())
+    return q, s
+
+
+def mod_quant_pack_a(x, weight, s_rows, t_rows, L, eps, rot_group=ROT_NONE, act_out=None, out=None):
+    """int8 of the modulated RMSNorm fp16(fp16(fp16(x*rstd*(w+1)) * s) + t) after an optional rotation.
+    x fp16 [M, K]; weight fp32 [K]; s_rows (= 1 + scale), t_rows fp16 [M // L, K]."""
+    require_cuda(x, weight, s_rows, t_rows)
+    _half2d(x, "x")
+    M, K = x.shape
+    for t, n in ((s_rows, "scale"), (t_rows, "shift")):
+        if t.dtype != torch.float16 or not t.is_contiguous() or t.numel() < ((M + L - 1) // L) * K:
+            raise RuntimeError(f"modulation {n} must be contiguous fp16 [M / L, K]")
+    if weight.dtype != torch.float32 or not weight.is_contiguous() or weight.numel() != K:
+        raise RuntimeError("norm weight must be contiguous fp32 [K]")
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=x.device),
+                                        torch.empty((M,), dtype=torch.float32, device=x.device))
+    call("b2_mod_quant_pack_a", ptr(x), I64(x.stride(0)), ptr(weight), ptr(s_rows), ptr(t_rows), I(L), F(eps), ptr(q),
+         ptr(s), I(M), I(K), I(rot_group), ptr(act_out), stream())
+    return q, s
+
+
+def gemm(a_q, a_scale, w_q, w_scale, bias=None, residual=None, gate=None, L=1, out=None):
+    """fp16 [M, N] = (a_q . w_q^T) * a_scale[m] * w_scale[n] (+ bias) (, residual + gate * y)."""
+    require_cuda(a_q, a_scale, w_q, w_scale, bias, residual, gate)
+    M, K = a_q.shape
+    N = w_q.shape[0]
+    if a_q.dtype != torch.int8 or w_q.dtype != torch.int8 or w_q.shape[1] != K:
+        raise RuntimeError("gemm operands must be int8 [M, K] and [N, K]")
+    if not (a_q.is_contiguous() and w_q.is_contiguous()):
+        raise RuntimeError("gemm operands must be contiguous")
+    if a_scale.dtype != torch.float32 or w_scale.dtype != torch.float32:
+        raise RuntimeError("gemm scales must be fp32")
+    if bias is not None and (bias.dtype != torch.float16 or not bias.is_contiguous()):
+        raise RuntimeError("gemm bias must be contiguous fp16")
+    if residual is not None:
+        if gate is None:
+            gate = torch.ones((1, N), dtype=torch.float16, device=a_q.device)
+            L = max(M, 1)
+        if residual.dtype != torch.float16 or not residual.is_contiguous() or residual.shape != (M, N):
+            raise RuntimeError("residual must be contiguous fp16 [M, N]")
+        if gate.dtype != torch.float16 or not gate.is_contiguous() or gate.shape[-1] != N:
+            raise RuntimeError("gate must be contiguous fp16 [M / L, N]")
+        if L < 1 or gate.numel() // N < (M + L - 1) // L:
+            raise RuntimeError(f"gate has {gate.numel() // N} rows, the {M} output rows need {(M + L - 1) // L} with L={L}")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=a_q.device)
+    call("b2_gemm", ptr(a_q), ptr(w_q), ptr(a_scale), ptr(w_scale.contiguous()), ptr(bias), ptr(out), I(M), I(N), I(K),
+         ptr(residual), ptr(gate if residual is not None else None), I(L), stream())
+    return out
+
+
+def gemm_i32(a_q, w_q):
+    """Raw int32 accumulators of the W8A8 kernel, [M, N]."""
+    require_cuda(a_q, w_q)
+    M, K = a_q.shape
+    N = w_q.shape[0]
+    out = torch.empty((M, N), dtype=torch.int32, device=a_q.device)
+    call("b2_gemm_i32", ptr(a_q.contiguous()), ptr(w_q.contiguous()), ptr(out), I(M), I(N), I(K), stream())
+    return out
+
+
+def attention(q, k, v, out, scale, int8_qk=False, workspace=None):
+    """Fused attention on (B, H, L, 128) fp16 views with a contiguous last dimension; writes ``out``."""
+    require_cuda(q, k, v, out)
+    B, H, Lq, D = q.shape
+    _, Hkv, Lk, _ = k.shape
+    if D != 128 or k.shape[-1] != 128 or v.shape[-1] != 128 or out.shape != q.shape:
+        raise RuntimeError("attention needs head dim 128 and out shaped like q")
+    for t in (q, k, v, out):
+        if t.dtype != torch.float16 or t.stride(-1) != 1:
+            raise RuntimeError("attention tensors must be fp16 with a contiguous last dimension")
+    ws_bytes = _lib.load().b2_attention_workspace_bytes(B, H, Hkv, Lq, Lk, int(bool(int8_qk)))
+    if ws_bytes and (workspace is None or workspace.numel() < ws_bytes):
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    call("b2_attention", ptr(q), *map(I64, q.stride()[:3]), ptr(k), *map(I64, k.stride()[:3]), ptr(v),
+         *map(I64, v.stride()[:3]), ptr(out), *map(I64, out.stride()[:3]), I(B), I(H), I(Hkv), I(Lq), I(Lk), F(scale),
+         I(int(bool(int8_qk))), ptr(workspace if ws_bytes else None), I64(ws_bytes), stream())
+    return out
+
+
+def rms_norm_rows(x, weight, eps, rows, D, L, H, sb, sh, sl, out, freqs=None, fb=0):
+    require_cuda(x, weight, out, freqs)
+    if freqs is None:
+        call("b2_rms_norm", ptr(x), ptr(weight), ptr(out), I(rows), I(D), I(L), I(H), I64(sb), I64(sh), I64(sl), F(eps),
+             stream())
+    else:
+        call("b2_rms_norm_rope", ptr(x), ptr(weight), ptr(out), I(rows), I(D), I(L), I(H), I64(sb), I64(sh), I64(sl),
+             F(eps), ptr(freqs), I64(fb), stream())
+    return out
+
+
+def rotate(x, group, out=None):
+    require_cuda(x)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise RuntimeError("rotate needs contiguous fp32")
+    out = torch.empty_like(x) if out is None else out
+    call("b2_rotate", ptr(x), ptr(out), I64(x.numel()), I(group), stream())
+    return out
+
+
+def gemv_i8(x, w, scale, bias=None, out=None):
+    """fp32 [N] = scale * (w int8 [N, K] . x fp32 [K]) (+ bias)."""
+    require_cuda(x, w, scale, bias)
+    N, K = w.shape
+    if x.dtype != torch.float32 or x.numel() != K or not x.is_contiguous():
+        raise RuntimeError("gemv_i8 needs one contiguous fp32 row of K values")
+    out = torch.empty((N,), dtype=torch.float32, device=x.device) if out is None else out
+    call("b2_gemv_i8", ptr(x), ptr(w), ptr(scale), ptr(bias), ptr(out), I(N), I(K), stream())
+    return out
+
+
+DECODE_SPLITS = 32
+
+
+def attn_decode(q, k, v, lengths, scale, out=None, partial=None, stats=None):
+    """q [B,1,H,128], k/v [B,cap,Hkv,128] fp32 contiguous, lengths int32 [B] on the device."""
+    require_cuda(q, k, v, lengths)
+    B, _, H, D = q.shape
+    _, cap, Hkv, _ = k.shape
+    q = q.contiguous()
+    out = torch.empty_like(q) if out is None else out
+    if partial is None:
+        partial = torch.empty((B * H, DECODE_SPLITS, 128), dtype=torch.float32, device=q.device)
+    if stats is None:
+        stats = torch.empty((B * H, DECODE_SPLITS, 2), dtype=torch.float32, device=q.device)
+    call("b2_attn_decode", ptr(q), ptr(k), ptr(v), ptr(lengths), ptr(out), ptr(partial), ptr(stats), I(B), I(H),
+         I(Hkv), I(cap), F(scale), stream())
+    return out
+
+
+def default_scale():
+    return 1.0 / math.sqrt(128)

@@ -1,0 +1,145 @@
+/*
+ * rdna2_b200.h — C-ABI of the B200 (sm_100a) kernels behind the drop-in Python modules.
+ *
+ * The reference binds its gfx1030 kernels by name through ctypes + hipModuleLaunchKernel
+ * (hip_attention.py:39-42): raw device pointers, int dims/strides and float scalars, launched on
+ * torch's current stream; buffers are allocated by the Python caller. These entry points keep that
+ * contract: plain pointers and sizes, a cudaStream_t passed as void*, no allocation inside, and an
+ * int status instead of a launch-time HIP error (hip_attention.py:14-16 raises RuntimeError on a
+ * non-zero code; the Python layer here does the same with b2_last_error()).
+ *
+ * All matrices are row-major. fp16 is IEEE binary16 passed as uint16_t bits.
+ */
+#ifndef RDNA2_B200_H
+#define RDNA2_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes. */
+#define B2_OK 0
+#define B2_ERR_INVALID 1     /* null pointer, negative size, inconsistent arguments */
+#define B2_ERR_UNSUPPORTED 2 /* shape or alignment outside what the kernel handles */
+#define B2_ERR_CUDA 3        /* CUDA runtime error at launch */
+#define B2_ERR_DEVICE 4      /* a kernel reported a device-side error (bounded wait expired) */
+
+/* Bits of the device status word returned by b2_device_status. */
+#define B2_DEV_TIMEOUT_PRODUCER 1u
+#define B2_DEV_TIMEOUT_MMA 2u
+#define B2_DEV_TIMEOUT_EPILOGUE 4u
+#define B2_DEV_TIMEOUT_DRAIN 8u
+
+/* Library version (major * 100 + minor). */
+int b2_version(void);
+
+/* Message of the last failing call on this host thread (empty string if none). */
+const char* b2_last_error(void);
+
+/* Synchronizes the current device, then returns in *flags and clears the status bits that kernels
+ * set when a bounded wait ran out. Returns B2_ERR_DEVICE if any bit was set. */
+int b2_device_status(unsigned int* flags);
+
+/* ------------------------------------------------------------------------------------------------
+ * Activation pre-pass: optional activation, optional block-Hadamard rotation, per-row int8.
+ * Replaces int8_gemm.hip quant_pack_a (:93), rot_quant_pack_a (:245), swiglu_rot_quant_pack_a
+ * (:253), gate_rot_quant_pack_a (:257) and mod_rot_quant_pack_a (:261), launched from
+ * int8_gemm.py:67 and :184. Output is plain row-major int8 [M, K] (ldq = K) and fp32 scale [M];
+ * the reference's packed register layout (int8_gemm.hip:41-58) is internal to its GEMM and not kept.
+ *
+ *   rot_group 0   : no rotation (quant_pack_a)
+ *   rot_group 256 : ConvRot H4^(x)4 / 16 over each 256 values (int8_gemm.hip:105-116,222-235)
+ *   rot_group 128 : Sylvester H2^(x)7 / sqrt(128) over each 128 values (block-128 configuration)
+ *
+ * Rounding (int8_gemm.hip:38,53): scale = max(absmax/127, 1e-30); q = clamp(floor(y/scale + 0.5)).
+ * act_out (nullable) receives the fp16 activation before rotation, for parity checks.
+ * x rows are ldx elements apart; element k of a row is at (k / seg) * seg_stride + k % seg when
+ * seg > 0 (a row gathered from per-rank segments), else at k.
+ * ------------------------------------------------------------------------------------------------ */
+int b2_quant_pack_a(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
+                    void* stream);
+int b2_quant_pack_a_seg(const uint16_t* x, int64_t ldx, int seg, int64_t seg_stride, int8_t* q, float* scale, int M,
+                        int K, int rot_group, void* stream);
+/* h = fp16(fp16(silu(gate)) * up), as F.silu(gate).mul_(up) (int8_gemm.hip:129-132). */
+int b2_swiglu_quant_pack_a(const uint16_t* gate, const uint16_t* up, int64_t ld, int8_t* q, float* scale, int M,
+                           int K, int rot_group, uint16_t* act_out, void* stream);
+/* h = fp16(x * fp16(sigmoid(gate))), as x * F.sigmoid(gate) (int8_gemm.hip:134-137). */
+int b2_gate_quant_pack_a(const uint16_t* x, const uint16_t* gate, int64_t ld, int8_t* q, float* scale, int M, int K,
+                         int rot_group, uint16_t* act_out, void* stream);
+/* h = fp16(fp16(fp16(x * rstd * (w + 1)) * s) + t), rstd = rsqrt(mean(x^2) + eps); s (= 1 + scale)
+ * and t are fp16 [M / L, K] rows (int8_gemm.hip:139-143,167-191; caller int8_gemm.py:176-186). */
+int b2_mod_quant_pack_a(const uint16_t* x, int64_t ldx, const float* w, const uint16_t* s, const uint16_t* t, int L,
+                        float eps, int8_t* q, float* scale, int M, int K, int rot_group, uint16_t* act_out,
+                        void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * W8A8 GEMM with fused epilogue. Replaces int8_gemm.hip gemm / gemm_k6144 (:411,:414) and the
+ * per-call pack_b (:271), launched from int8_gemm.py:70-79. B is the weight as stored, int8 [N, K].
+ *   y = (float)acc * as[m] * ws[n] (+ bias[n])  -> fp16                     (int8_gemm.hip:382-383)
+ *   with R: out = fp16(R[m,n] + fp16(G[m / L, n] * y))                      (int8_gemm.hip:394-400)
+ * Needs K % 16 == 0, N % 8 == 0, 16-byte aligned A and B.
+ * ------------------------------------------------------------------------------------------------ */
+int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const float* ws, const uint16_t* bias, uint16_t* C,
+            int M, int N, int K, const uint16_t* R, const uint16_t* G, int L, void* stream);
+/* Raw int32 accumulators C32[M, N] = A B^T of the same kernel, for bit-exact checks. */
+int b2_gemm_i32(const int8_t* A, const int8_t* B, int32_t* C32, int M, int N, int K, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Fused attention, head dim 128, no mask. Replaces hip_attention.hip pack_kv + attn (:32,:280) and
+ * pack_kv_i8 + attn_i8 (:59,:161), launched from hip_attention.py:48-66 (called by attention.py:46-61).
+ * q [B,H,Lq,128], k/v [B,Hkv,Lk,128], out [B,H,Lq,128], fp16, any element strides (b, h, l) that are
+ * multiples of 8 with a contiguous last dimension; H % Hkv == 0 (grouped-query heads share K/V).
+ * int8_qk != 0 selects per-row int8 Q and per-key int8 K with int32 dot products and fp16 PV; it needs
+ * b2_attention_workspace_bytes() of caller-provided device scratch (16-byte aligned), else none.
+ * ------------------------------------------------------------------------------------------------ */
+int64_t b2_attention_workspace_bytes(int B, int H, int Hkv, int Lq, int Lk, int int8_qk);
+int b2_attention(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k, int64_t skb,
+                 int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl, uint16_t* out,
+                 int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk, float scale,
+                 int int8_qk, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * RMSNorm with fp32 math, zero-centred fp32 weight: y = fp16(x * rsqrt(mean(x^2) + eps) * (w + 1)).
+ * Replaces rms_norm.hip rms_norm_head / rms_norm_row (:67,:71), launched from rms_norm.py:36.
+ * Rows are ordered head-first: row n -> (h = n % H, l = (n / H) % L, b = n / (H L)), read from
+ * x + b sb + h sh + l sl, written contiguous as [B, H, L, D]. D % 8 == 0, D <= 8192.
+ * ------------------------------------------------------------------------------------------------ */
+int b2_rms_norm(const uint16_t* x, const float* w, uint16_t* y, int rows, int D, int L, int H, int64_t sb, int64_t sh,
+                int64_t sl, float eps, void* stream);
+/* RMSNorm + rope over 128-wide heads (rms_norm.hip:48-61,75-77; rms_norm.py:42-52): F holds per token
+ * 64 pairs of 2x2 fp32 rotations [fb-strided batch][L][64][2][2]. */
+int b2_rms_norm_rope(const uint16_t* x, const float* w, uint16_t* y, int rows, int D, int L, int H, int64_t sb,
+                     int64_t sh, int64_t sl, float eps, const float* F, int64_t fb, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Single-token decode (int8_gemv.hip, launched from int8_gemv.py).
+ * ------------------------------------------------------------------------------------------------ */
+/* fp32 regular-Hadamard rotation of each `group` values (power of 4), times rsqrt(group)
+ * (int8_gemv.hip:108-129 rotate; int8_gemv.py:42-45). n % group == 0. */
+int b2_rotate(const float* x, float* out, int64_t n, int group, void* stream);
+/* out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32 (int8_gemv.hip:131-162 gemv_i8;
+ * int8_gemv.py:62-63). K % 16 == 0. */
+int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
+               void* stream);
+/* fp32 split-KV decode attention + merge (int8_gemv.hip:198-271 attn_decode/attn_merge;
+ * int8_gemv.py:101-114). q [B,1,H,128], k/v [B,capacity,Hkv,128], lengths int32 [B] read on the
+ * device (graph-replayable), out [B,1,H,128]. partial: fp32 [B*H, 32, 128], stats: fp32 [B*H, 32, 2]
+ * scratch from the caller. */
+int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out, float* partial,
+                   float* stats, int batch, int heads, int kv_heads, int capacity, float scale, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RDNA2_B200_H */

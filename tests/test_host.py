@@ -1,0 +1,139 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every declared entry point, argument
+validation returns the documented status codes before touching the device, and the drop-in modules' host logic
+(eligibility, ConvRot hand-off, patch installation) behaves like the reference's."""
+import ctypes
+import os
+import re
+import sys
+import types
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "rdna2_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b2_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._lib.load()
+    names = declared_symbols()
+    assert len(names) >= 17
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(pkg._lib.SIGNATURES), "ctypes signatures and header disagree"
+    assert lib.b2_version() == 100
+
+
+def _status(pkg, name, *args):
+    return getattr(pkg._lib.load(), name)(*args)
+
+
+def test_validation_errors_before_any_launch(pkg):
+    P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    fake = P(4096)
+    # null pointers -> B2_ERR_INVALID
+    assert _status(pkg, "b2_gemm", P(None), fake, fake, fake, P(None), fake, I(8), I(8), I(16), P(None), P(None), I(1), P(None)) == 1
+    assert b"null" in pkg._lib.load().b2_last_error()
+    # K not a multiple of 16 -> B2_ERR_UNSUPPORTED
+    assert _status(pkg, "b2_gemm_i32", fake, fake, fake, I(8), I(8), I(24), P(None)) == 2
+    assert _status(pkg, "b2_quant_pack_a", fake, I64(24), fake, fake, I(4), I(24), I(0), P(None)) == 2
+    # rotation group must divide K
+    assert _status(pkg, "b2_quant_pack_a", fake, I64(384), fake, fake, I(4), I(384), I(256), P(None)) == 2
+    assert _status(pkg, "b2_quant_pack_a", fake, I64(512), fake, fake, I(4), I(512), I(64), P(None)) == 2
+    # misaligned operand
+    assert _status(pkg, "b2_gemm_i32", P(4097), fake, fake, I(8), I(8), I(16), P(None)) == 2
+    # rotate: group must be a power of 4
+    assert _status(pkg, "b2_rotate", fake, fake, I64(128), I(128), P(None)) == 2
+    # decode attention: heads must be a multiple of kv heads
+    assert _status(pkg, "b2_attn_decode", fake, fake, fake, fake, fake, fake, fake, I(1), I(6), I(4), I(16), F(1.0), P(None)) == 1
+    # attention: head counts
+    assert _status(pkg, "b2_attention", fake, I64(0), I64(0), I64(128), fake, I64(0), I64(0), I64(128), fake, I64(0), I64(0),
+                   I64(128), fake, I64(0), I64(0), I64(128), I(1), I(3), I(2), I(4), I(4), F(1.0), I(0), P(None), I64(0), P(None)) == 1
+    # rms_norm: D bound
+    assert _status(pkg, "b2_rms_norm", fake, fake, fake, I(1), I(8200), I(1), I(1), I64(0), I64(0), I64(8200), F(1e-6), P(None)) == 2
+    # empty problems succeed without launching
+    assert _status(pkg, "b2_gemm_i32", fake, fake, fake, I(0), I(8), I(16), P(None)) == 0
+    assert _status(pkg, "b2_quant_pack_a", fake, I64(16), fake, fake, I(0), I(16), I(0), P(None)) == 0
+
+
+def test_attention_workspace_size(pkg):
+    lib = pkg._lib.load()
+    assert lib.b2_attention_workspace_bytes(2, 24, 24, 4056, 4056, 0) == 0
+    n = lib.b2_attention_workspace_bytes(2, 24, 24, 4056, 4056, 1)
+    assert n >= 2 * (2 * 24 * 4056 * 128) + 2 * 2 * 24 * 4056 * 4
+    assert n % 1024 == 0
+
+
+def test_cpu_tensors_are_refused(pkg):
+    x = torch.zeros((4, 256), dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        pkg.ops.quant_pack_a(x, 256)
+
+
+def test_attention_hip_refuses_ineligible_inputs(pkg):
+    q = torch.zeros((1, 8, 2 * 128), dtype=torch.float16)
+    with pytest.raises(NotImplementedError, match="mask"):
+        pkg.attention.attention_hip(q, q, q, 2, mask=torch.zeros(1))
+    with pytest.raises(NotImplementedError, match="head dim 64"):
+        pkg.attention.attention_hip(q, q, q, 4)
+    with pytest.raises(NotImplementedError, match="fp16"):
+        pkg.attention.attention_hip(q.float(), q.float(), q.float(), 2)
+    assert pkg.attention.eligible(q, q, q, 2) is None
+
+
+def test_int8_linear_refuses_ineligible_inputs(pkg):
+    f = pkg.int8_gemm.wrap(None)
+    w = torch.zeros((64, 64), dtype=torch.int8)
+    with pytest.raises(NotImplementedError, match="x_q"):
+        f(torch.zeros((4, 64), dtype=torch.float16), w, 1.0, x_q=torch.zeros(1))
+    with pytest.raises(NotImplementedError, match="fp16"):
+        f(torch.zeros((4, 64)), w, 1.0)
+
+
+def _fake_packs():
+    pack = types.ModuleType("fakepack.int8_quant")
+    pack.triton_int8_linear = lambda *a, **k: "orig"
+    pack.triton_int8_linear_per_row = lambda *a, **k: "orig_row"
+    pack._TRITON_AVAILABLE = True
+
+    class Linear:
+        def forward(self, x):
+            return "forward"
+
+    pack.Int8TensorwiseOps = types.SimpleNamespace(Linear=Linear)
+    convrot = types.ModuleType("fakepack.convrot")
+    convrot.rotate_activation = lambda x, H, g: ("rotated", x)
+    convrot.build_hadamard = lambda n, device=None, dtype=None: None
+    return pack, convrot
+
+
+def test_enable_installs_and_removes_patches(pkg):
+    g = pkg.int8_gemm
+    pack, convrot = _fake_packs()
+    sys.modules["fakepack.int8_quant"], sys.modules["fakepack.convrot"] = pack, convrot
+    try:
+        g.originals.clear()
+        g.enable(True)
+        assert pack.triton_int8_linear.__name__ == "int8_linear"
+        assert convrot.rotate_activation is g.rotate_activation
+        assert g.swiglu_fusable
+        # ConvRot hand-off: a fusable 2D fp16 activation is parked, not rotated.
+        x = torch.zeros((4, 512), dtype=torch.float16)
+        g.fusable = True
+        assert g.rotate_activation(x, None, 256) is x and g.pending is x
+        g.fusable, g.pending = False, None
+        assert g.rotate_activation(x, None, 256)[0] == "rotated"
+        g.enable(False)
+        assert pack.triton_int8_linear() == "orig" and convrot.rotate_activation(x, None, 256)[0] == "rotated"
+        assert not g.swiglu_fusable
+    finally:
+        del sys.modules["fakepack.int8_quant"], sys.modules["fakepack.convrot"]
+        g.originals.clear()
+        g.pending = None
+        g.fusable = False

@@ -1,0 +1,123 @@
+"""Pre-pass parity on the GPU: int8 activations and fp32 scales bit-exact against the oracle (int8_gemm.hip
+quant/rotation semantics). Stages with exp/rsqrt are checked to one fp16 step, then bit-exact downstream of the
+kernel's own fp16 activation."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+F16 = np.float16
+
+
+def dev_(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def activations(M, K, seed, outliers=True):
+    g = np.random.default_rng(seed)
+    x = g.standard_normal((M, K)).astype(np.float32)
+    if outliers:
+        ch = g.choice(K, max(1, K // 100), replace=False)
+        x[:, ch] *= 20
+    return x.astype(F16)
+
+
+SHAPES = [(1, 256), (7, 512), (64, 3072), (130, 1024), (33, 640), (5, 16384), (300, 8192)]
+
+
+@pytest.mark.parametrize("rot", [0, 128, 256])
+@pytest.mark.parametrize("M,K", SHAPES)
+def test_quant_bit_exact(pkg, dev, rot, M, K):
+    if rot and K % rot:
+        pytest.skip("K not a multiple of the rotation group")
+    x = activations(M, K, M * 7 + K)
+    q, s = pkg.ops.quant_pack_a(dev_(x, dev), rot)
+    q_ref, s_ref, _ = oq.prepass(x, rot)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
+def test_quant_edge_values(pkg, dev):
+    K = 256
+    x = np.zeros((6, K), F16)
+    x[1, :] = 65504                      # fp16 max
+    x[2, ::2] = 6e-8                     # subnormal fp16
+    x[3, :8] = [127, 0.5, -0.5, 1.5, -1.5, 2.5, -2.5, -127]  # half-up ties with scale 1
+    x[4] = np.linspace(-3, 3, K).astype(F16)
+    x[5, 17] = -1
+    for rot in (0, 128, 256):
+        q, s = pkg.ops.quant_pack_a(dev_(x, dev), rot)
+        q_ref, s_ref, _ = oq.prepass(x, rot)
+        assert np.array_equal(s.cpu().numpy(), s_ref), rot
+        assert np.array_equal(q.cpu().numpy(), q_ref), rot
+    q, _ = pkg.ops.quant_pack_a(dev_(x, dev), 0)
+    assert q.cpu().numpy()[3, :8].tolist() == [127, 1, 0, 2, -1, 3, -2, -127]
+
+
+def test_quant_strided_rows(pkg, dev):
+    big = activations(40, 1024, 3)
+    x = dev_(big, dev)[:, 256:768]  # row stride 1024, 512 values per row
+    q, s = pkg.ops.quant_pack_a(x, 256)
+    q_ref, s_ref, _ = oq.prepass(big[:, 256:768], 256)
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def test_quant_gathered_segments(pkg, dev):
+    # A row gathered from 4 per-rank segments [g, T, 384]: element k at (k // 384) * T * 384 + t * 384 + k % 384.
+    g_, T, w = 4, 50, 384
+    parts = activations(g_ * T, w, 4).reshape(g_, T, w)
+    x = dev_(parts, dev)
+    q, s = pkg.ops.quant_pack_a_segments(x, g_ * w, 128, w, T * w, T, w)
+    full = parts.transpose(1, 0, 2).reshape(T, g_ * w)
+    q_ref, s_ref, _ = oq.prepass(full, 128)
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def _check_act(pkg, dev, act16, ref16, q, s, rot):
+    a = act16.cpu().numpy()
+    diff = np.abs(a.astype(np.float32) - ref16.astype(np.float32))
+    ulp = np.abs(np.spacing(ref16.astype(F16)).astype(np.float32))
+    assert np.all(diff <= ulp), "activation off by more than one fp16 step"
+    assert np.mean(a != ref16) < 2e-3
+    q_ref, s_ref = oq.quant_rows(oq.rotate_rows(a, rot))
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
+@pytest.mark.parametrize("rot", [0, 128, 256])
+def test_swiglu_prepass(pkg, dev, rot):
+    M, K = 97, 8192
+    g = np.random.default_rng(11)
+    gate = (g.standard_normal((M, K)) * 2).astype(F16)
+    up = g.standard_normal((M, K)).astype(F16)
+    act = torch.empty((M, K), dtype=torch.float16, device=dev)
+    q, s = pkg.ops.swiglu_quant_pack_a(dev_(gate, dev), dev_(up, dev), rot, act_out=act)
+    _check_act(pkg, dev, act, oq.swiglu(gate, up), q, s, rot)
+
+
+@pytest.mark.parametrize("rot", [0, 256])
+def test_gate_prepass(pkg, dev, rot):
+    M, K = 65, 3072
+    g = np.random.default_rng(12)
+    x = g.standard_normal((M, K)).astype(F16)
+    gate = (g.standard_normal((M, K)) * 3).astype(F16)
+    act = torch.empty((M, K), dtype=torch.float16, device=dev)
+    q, s = pkg.ops.gate_quant_pack_a(dev_(x, dev), dev_(gate, dev), rot, act_out=act)
+    _check_act(pkg, dev, act, oq.sigmoid_gate(x, gate), q, s, rot)
+
+
+@pytest.mark.parametrize("rot", [0, 128, 256])
+def test_mod_prepass(pkg, dev, rot):
+    B, L, K = 2, 131, 3072
+    g = np.random.default_rng(13)
+    x = activations(B * L, K, 14)
+    w = (g.standard_normal(K) * 0.02).astype(np.float32)
+    s_rows = (1 + g.standard_normal((B, K)) * 0.1).astype(F16)
+    t_rows = (g.standard_normal((B, K)) * 0.1).astype(F16)
+    act = torch.empty((B * L, K), dtype=torch.float16, device=dev)
+    q, s = pkg.ops.mod_quant_pack_a(dev_(x, dev), dev_(w, dev), dev_(s_rows, dev), dev_(t_rows, dev), L, 1e-6, rot,
+                                    act_out=act)
+    _check_act(pkg, dev, act, oq.modulate(x, w, s_rows, t_rows, L, 1e-6), q, s, rot)
