@@ -67,6 +67,11 @@ class Clocks:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, timeout=3.0):
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.05)
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -316,7 +321,163 @@ class AttnC2:
         return flops / dt / 1e12, f"{reps} single (batch, head) slices of C2 through the reference's attention_bmm (fp16 CPU), scaled per slice"
 
 
-WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True)}
+class KindTimer:
+    """Records CUDA events around each launch of a kind ("gemm", "attention", ...) during one instrumented step."""
+
+    def __init__(self):
+        self.active = False
+        self.records = []
+
+    def __call__(self, kind, work=0):
+        timer = self
+
+        class _Ctx:
+            def __enter__(self):
+                if timer.active:
+                    self.e0 = torch.cuda.Event(enable_timing=True)
+                    self.e0.record()
+
+            def __exit__(self, *exc):
+                if timer.active:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record()
+                    timer.records.append((kind, work, self.e0, e1))
+
+        return _Ctx()
+
+    def summary(self):
+        torch.cuda.synchronize()
+        out = {}
+        for kind, work, e0, e1 in self.records:
+            d = out.setdefault(kind, {"ms": 0.0, "work": 0.0, "launches": 0})
+            d["ms"] += e0.elapsed_time(e1)
+            d["work"] += work
+            d["launches"] += 1
+        return out
+
+
+class DiTC4:
+    name = "dit"
+    metric = "DiT-block ms/step (C4: 8 W8A8 DiT blocks, B2 CFG x 3321 tokens, hidden 3072, 24 heads, MLP 8192)"
+    unit = "ms/step"
+    higher = False
+
+    def __init__(self, dev, world=1, rank=0):
+        import importlib
+
+        p = pkg()
+        dit = importlib.import_module(p.__name__ + ".dit")
+        self.cfg = cfg = dit.DiTConfig()
+        self.plan = plan = dit.shard_plan(world, rank, cfg.batch, cfg.heads)
+        pg = None
+        if world > 1:
+            groups = {}
+            for r in range(world):
+                gr = dit.shard_plan(world, r, cfg.batch, cfg.heads).group_ranks
+                if gr not in groups:
+                    groups[gr] = dist.new_group(list(gr)) if len(gr) > 1 else None
+            pg = groups[plan.group_ranks]
+        gather = (lambda out, inp: dist.all_gather_into_tensor(out, inp, group=pg)) if pg is not None else None
+        self.timer = KindTimer()
+        self.stack = dit.DiTStack(cfg, plan, dev, seed=0, all_gather=gather, timer=self.timer)
+        b = plan.batch_hi - plan.batch_lo
+        gen = torch.Generator().manual_seed(4)
+        x_all = torch.randn((cfg.batch, cfg.tokens, cfg.hidden), generator=gen).half()
+        self.x_host = x_all[plan.batch_lo:plan.batch_hi].contiguous().pin_memory()
+        self.x0 = self.x_host.to(dev)
+        self.x = torch.empty_like(self.x0)
+        self.out_host = torch.empty_like(self.x_host).pin_memory()
+        self.world = world
+        self.lin_ops, self.att_flops = self.stack.flops()
+        self.launches_per_step = cfg.blocks * self.stack.launches_per_block
+        self.events = []
+        self.components = None
+        self.config = {"workload": "C4 DiT block stack", "blocks": 8, "batch": 2, "tokens": 3321, "hidden": 3072,
+                       "heads": 24, "mlp": 8192, "weights": "W8A8 per-channel int8, block-128 Hadamard",
+                       "l2": "weights 0.9 GB per step, inputs larger than L2",
+                       "shard": {"branches": [plan.batch_lo, plan.batch_hi], "heads": [plan.head_lo, plan.head_hi],
+                                 "group": list(plan.group_ranks)}}
+
+    def step(self, i, record=False):
+        self.x.copy_(self.x0)
+        self.timer.active = record
+        if record:
+            self.timer.records = []
+        self.stack.forward(self.x)
+        if record:
+            self.components = self.timer.summary()
+            self.timer.active = False
+            g = self.components.get("gemm")
+            if g:
+                self.events = [(None, None)]
+                self.gemm_ms, self.gemm_ops = g["ms"], g["work"]
+
+    def e2e_step(self, i):
+        self.x.copy_(self.x_host, non_blocking=True)
+        self.stack.forward(self.x)
+        self.out_host.copy_(self.x, non_blocking=True)
+
+    h2d_bytes = property(lambda self: self.x_host.numel() * 2)
+    d2h_bytes = property(lambda self: self.x_host.numel() * 2)
+
+    def value(self, ms, steps, world):
+        return ms / steps
+
+    def roofline(self, peaks, kms):
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        achieved = self.gemm_ops / (self.gemm_ms * 1e-3) / 1e12
+        comp = {}
+        for kind, d in (self.components or {}).items():
+            c = {"ms": d["ms"], "launches": d["launches"]}
+            if kind == "gemm":
+                c["TOPS"] = d["work"] / (d["ms"] * 1e-3) / 1e12
+            if kind == "attention":
+                c["TFLOPS"] = d["work"] / (d["ms"] * 1e-3) / 1e12
+                c["frac_of_fp16_peak"] = c["TFLOPS"] / peaks["bf16_tflops"]
+            comp[kind] = c
+        step_roof_ms = (self.lin_ops / (int8_peak * 1e12) + self.att_flops / (peaks["bf16_tflops"] * 1e12)) * 1e3
+        return {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
+                "traffic": None, "kernel": "gemm_w8a8_kernel (all 32 GEMM launches of a step)",
+                "note": f"int8 peak = 2 x {peaks['source']} bf16 ({peaks['bf16_tflops']} TFLOP/s)",
+                "components": comp, "step_roofline_ms": step_roof_ms}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        """One block of the reference's CPU path on a sample (512 of the 6642 rows through the W8A8 linears, 2 of the 48
+        (batch, head) attention slices through attention_bmm), scaled to the 8-block step."""
+        from oracle import attention as oatt
+        from oracle import gemm as ogemm
+        from oracle import quant as oq
+
+        torch.set_num_threads(threads)
+        g = np.random.default_rng(0)
+        D, F, T, Ms = 3072, 8192, 3321, 512
+        w = {n: g.integers(-127, 128, s, dtype=np.int8) for n, s in
+             {"qkv": (3 * D, D), "o": (D, D), "gu": (2 * F, D), "down": (D, F)}.items()}
+        ws = {n: np.full(v.shape[0], 1e-3, np.float32) for n, v in w.items()}
+        x = g.standard_normal((Ms, D)).astype(np.float16)
+        ones, zeros = np.ones((1, D), np.float16), np.zeros((1, D), np.float16)
+        nw = np.zeros(D, np.float32)
+        t0 = time.perf_counter()
+        q, s = oq.quant_rows(oq.rotate_rows(oq.modulate(x, nw, ones, zeros, Ms, 1e-6), 128))
+        ogemm.epilogue(ogemm.int_mm(q, w["qkv"]), s, ws["qkv"])
+        q, s = oq.quant_rows(oq.rotate_rows(x, 128))
+        xa = ogemm.epilogue(ogemm.int_mm(q, w["o"]), s, ws["o"], R=x, G=ones, L=Ms)
+        q, s = oq.quant_rows(oq.rotate_rows(oq.modulate(xa, nw, ones, zeros, Ms, 1e-6), 128))
+        gu = ogemm.epilogue(ogemm.int_mm(q, w["gu"]), s, ws["gu"])
+        q, s = oq.quant_rows(oq.rotate_rows(oq.swiglu(gu[:, :F], gu[:, F:]), 128))
+        ogemm.epilogue(ogemm.int_mm(q, w["down"]), s, ws["down"], R=xa, G=ones, L=Ms)
+        t_lin = time.perf_counter() - t0
+        gen = torch.Generator().manual_seed(2)
+        qa, ka, va = (torch.randn((1, 2, T, 128), generator=gen).half() for _ in range(3))
+        t0 = time.perf_counter()
+        oatt.attention_bmm(qa, ka, va)
+        t_att = time.perf_counter() - t0
+        ms = 8 * (t_lin * (2 * T / Ms) + t_att * (48 / 2)) * 1e3
+        return ms, "one block: 512 of 6642 rows through the 4 W8A8 linears (oracle pre-pass + torch._int_mm + epilogue) and 2 of 48 (batch, head) attention slices (attention_bmm, fp16), scaled to 8 blocks"
+
+
+WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4}
 
 
 def reference_arm(args, world, rank):
@@ -333,6 +494,11 @@ def reference_arm(args, world, rank):
         metric = f"attention TFLOPS (C2: B2 H24 S4056 d128, {'int8' if name == 'attn_i8' else 'fp16'} QK)"
         unit, higher = "TFLOPS", True
         cfg = {"workload": "C2 fused attention", "B": 2, "H": 24, "S": 4056, "d": 128}
+    elif name == "dit":
+        v, sample = DiTC4.cpu_baseline(threads)
+        metric, unit, higher = DiTC4.metric, DiTC4.unit, False
+        cfg = {"workload": "C4 DiT block stack", "blocks": 8, "batch": 2, "tokens": 3321, "hidden": 3072, "heads": 24,
+               "mlp": 8192}
     else:
         print(json.dumps({"impl": "reference", "unavailable": f"no CPU reference arm for workload {name}"}))
         return
@@ -349,7 +515,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="gemm", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="dit", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -360,7 +526,8 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peaks = load_peaks()
-    wl = WORKLOADS[args.workload](dev)
+    ctor = WORKLOADS[args.workload]
+    wl = ctor(dev, world, rank) if ctor is DiTC4 else ctor(dev)
 
     # Kernel timing pass (dominant kernel), then the timed whole-job pass, then the end-to-end pass.
     for i in range(args.warmup):
@@ -368,16 +535,25 @@ def main():
     wl.events = []
     for i in range(args.steps):
         wl.step(i, record=True)
-    kms = kernel_ms(wl.events)
+    kms = kernel_ms(wl.events) if not isinstance(wl, DiTC4) else None
 
     with Clocks(local) as clocks:
+        # Pre-roll under the sampler so that the clock record covers the load of the timed region that follows.
+        clocks.wait_first()
+        t_end, i = time.time() + 1.0, 0
+        while time.time() < t_end:
+            wl.step(i)
+            torch.cuda.synchronize()
+            i += 1
         ms = timed(wl.step, args.steps, args.warmup, world)
     e2e_ms = timed(wl.e2e_step, args.steps, args.warmup, world)
 
     line = {"metric": wl.metric, "value": wl.value(ms, args.steps, world), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": wl.higher, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp16",
-            "data": "synthetic (seeded, BASELINE shapes)", "config": dict(wl.config, parallelism=f"replicas x{world}"),
+            "higher_is_better": wl.higher, "scaling": "strong" if isinstance(wl, DiTC4) else "weak",
+            "vs_baseline": None, "dtype": "int8/fp16", "data": "synthetic (seeded, BASELINE shapes, random-init weights)",
+            "config": dict(wl.config, parallelism=(f"cfg x{min(world, 2)} heads x{max(1, world // 2)}" if isinstance(wl, DiTC4)
+                                                   else f"replicas x{world}")),
             "e2e": {"value": wl.value(e2e_ms, args.steps, world), "unit": wl.unit,
                     "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
             "roofline": wl.roofline(peaks, kms), "kernel_ms": kms, "clocks": clocks.summary(),

@@ -64,7 +64,7 @@ def quant_rows_rint(x):
     f = np.asarray(x).astype(F32)
     mx = np.abs(f).max(axis=-1)
     scale = np.maximum(mx / F32(127), F32(1e-30)).astype(F32)
-    q = np.clip(np.rint(f / scale[..., None]), -128, 127).astype(np.int8)
+    q = np.fmin(np.fmax(np.rint(f / scale[..., None]), F32(-128)), F32(127)).astype(np.int8)
     return q, scale
 
 

@@ -21,8 +21,10 @@ def quant_rows(y):
     f = np.asarray(y).astype(F32)
     mx = np.abs(f).max(axis=1) if f.shape[1] else np.zeros(f.shape[0], F32)
     scale = np.maximum(mx / F32(127), F32(1e-30)).astype(F32)
-    q = np.floor(f / scale[:, None] + F32(0.5))
-    return np.clip(q, -128, 127).astype(np.int8), scale
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = np.floor(f / scale[:, None] + F32(0.5))
+    # fminf(fmaxf(q, -128), 127): IEEE maxNum/minNum drop a NaN operand (inf / inf after an fp16 overflow).
+    return np.fmin(np.fmax(q, F32(-128)), F32(127)).astype(np.int8), scale
 
 
 def _h4(a, b, c, d):
@@ -62,7 +64,8 @@ def hadamard128(x):
         a = np.take(v, 0, axis=axis)
         b = np.take(v, 1, axis=axis)
         v = np.stack((a + b, a - b), axis=axis)
-    return (v.reshape(M, K) * INV_SQRT128).astype(F16)
+    with np.errstate(over="ignore"):
+        return (v.reshape(M, K) * INV_SQRT128).astype(F16)
 
 
 def rotate_rows(y16, rot_group):
