@@ -321,6 +321,87 @@ class AttnC2:
         return flops / dt / 1e12, f"{reps} single (batch, head) slices of C2 through the reference's attention_bmm (fp16 CPU), scaled per slice"
 
 
+class W4A8C3:
+    name = "w4a8"
+    metric = "W4A8 GEMM TOPS (C3: 2809x3072x8192, int4 weights, group-128 fp16 scales, pre-pass + GEMM)"
+    unit = "TOPS"
+    higher = True
+    M, K, N = 2809, 3072, 8192
+
+    def __init__(self, dev):
+        from oracle import weights as ow
+
+        p = pkg()
+        self.ops = p.ops
+        g = np.random.default_rng(3)
+        x = g.standard_normal((self.M, self.K)).astype(np.float16)
+        self.x_host = torch.from_numpy(x).pin_memory()
+        w = (g.standard_normal((self.N, self.K)) * 0.02).astype(np.float32)
+        packed, s16 = ow.quantize_int4_groups(ow.sylvester_rotate(w))
+        per = self.M * self.K * 3 + self.N * self.K // 2 + self.M * self.N * 2
+        self.sets = max(2, math.ceil(2 * L2_BYTES / per))
+        self.xs = [self.x_host.to(dev) for _ in range(self.sets)]
+        self.ws = [torch.from_numpy(packed).to(dev) for _ in range(self.sets)]
+        self.gs = self.ops.w4a8_scales(torch.from_numpy(s16).to(dev))
+        self.qs = [(torch.empty((self.M, self.K), dtype=torch.int8, device=dev),
+                    torch.empty((self.M,), dtype=torch.float32, device=dev)) for _ in range(self.sets)]
+        self.outs = [torch.empty((self.M, self.N), dtype=torch.float16, device=dev) for _ in range(self.sets)]
+        self.y_host = torch.empty((self.M, self.N), dtype=torch.float16).pin_memory()
+        self.events = []
+        self.launches_per_step = 2
+        self.ops_per_step = 2.0 * self.M * self.N * self.K
+        self.config = {"workload": "C3 W4A8 linear", "M": self.M, "K": self.K, "N": self.N, "group": 128,
+                       "rotation": "block-128 Sylvester", "l2": "rotating input/weight sets > 2x L2"}
+
+    def step(self, i, record=False):
+        s = i % self.sets
+        q = self.ops.quant_pack_a(self.xs[s], 128, out=self.qs[s])
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.ops.gemm_w4a8(q[0], q[1], self.ws[s], self.gs, out=self.outs[s])
+        if record:
+            e1.record()
+            self.events.append((e0, e1))
+
+    def e2e_step(self, i):
+        s = i % self.sets
+        x = self.x_host.to(self.xs[s].device, non_blocking=True)
+        q = self.ops.quant_pack_a(x, 128)
+        y = self.ops.gemm_w4a8(q[0], q[1], self.ws[s], self.gs)
+        self.y_host.copy_(y, non_blocking=True)
+
+    h2d_bytes = property(lambda self: self.M * self.K * 2)
+    d2h_bytes = property(lambda self: self.M * self.N * 2)
+
+    def value(self, ms, steps, world):
+        return self.ops_per_step * steps * world / (ms * 1e-3) / 1e12
+
+    def roofline(self, peaks, kms):
+        peak = 2.0 * peaks["bf16_tflops"]
+        achieved = self.ops_per_step / (kms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS", "frac": achieved / peak,
+                "traffic": None, "kernel": "gemm_w4a8_kernel",
+                "note": f"int8 peak = 2 x {peaks['source']} bf16 ({peaks['bf16_tflops']} TFLOP/s)"}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        from oracle import gemm as ogemm
+        from oracle import quant as oq
+        from oracle import weights as ow
+
+        torch.set_num_threads(threads)
+        g = np.random.default_rng(3)
+        M, K, N = 512, W4A8C3.K, W4A8C3.N
+        x = g.standard_normal((M, K)).astype(np.float16)
+        packed, s16 = ow.quantize_int4_groups((g.standard_normal((N, K)) * 0.02).astype(np.float32))
+        t0 = time.perf_counter()
+        q, s, _ = oq.prepass(x, 128)
+        ogemm.w4a8_grouped(q, s, packed, s16)
+        dt = time.perf_counter() - t0
+        return 2.0 * M * N * K / dt / 1e12, "512 of the 2809 rows through the oracle pre-pass + per-group torch._int_mm + fp32 combine"
+
+
 class KindTimer:
     """Records CUDA events around each launch of a kind ("gemm", "attention", ...) during one instrumented step."""
 
@@ -477,7 +558,8 @@ class DiTC4:
         return ms, "one block: 512 of 6642 rows through the 4 W8A8 linears (oracle pre-pass + torch._int_mm + epilogue) and 2 of 48 (batch, head) attention slices (attention_bmm, fp16), scaled to 8 blocks"
 
 
-WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4}
+WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4,
+             "w4a8": W4A8C3}
 
 
 def reference_arm(args, world, rank):
@@ -494,6 +576,10 @@ def reference_arm(args, world, rank):
         metric = f"attention TFLOPS (C2: B2 H24 S4056 d128, {'int8' if name == 'attn_i8' else 'fp16'} QK)"
         unit, higher = "TFLOPS", True
         cfg = {"workload": "C2 fused attention", "B": 2, "H": 24, "S": 4056, "d": 128}
+    elif name == "w4a8":
+        v, sample = W4A8C3.cpu_baseline(threads)
+        metric, unit, higher, cfg = W4A8C3.metric, W4A8C3.unit, True, {"workload": "C3 W4A8 linear", "M": 2809,
+                                                                         "K": 3072, "N": 8192, "group": 128}
     elif name == "dit":
         v, sample = DiTC4.cpu_baseline(threads)
         metric, unit, higher = DiTC4.metric, DiTC4.unit, False

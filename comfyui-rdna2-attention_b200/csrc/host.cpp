@@ -86,7 +86,7 @@ const char* b2_last_error(void) { return b2::g_message; }
 int b2_device_status(unsigned int* flags) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return b2::fail(B2_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
-    unsigned int f = b2::read_status_gemm() | b2::read_status_attention();
+    unsigned int f = b2::read_status_gemm() | b2::read_status_attention() | b2::read_status_gemm_w4a8();
     if (flags) *flags = f;
     if (f) return b2::fail(B2_ERR_DEVICE, "device status 0x%x: a bounded wait ran out", f);
     return B2_OK;

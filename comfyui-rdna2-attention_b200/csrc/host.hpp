@@ -52,5 +52,6 @@ inline int set_smem(K kernel, int bytes) {
 // Per-translation-unit device status words, read and cleared by b2_device_status().
 unsigned int read_status_gemm();
 unsigned int read_status_attention();
+unsigned int read_status_gemm_w4a8();
 
 }  // namespace b2

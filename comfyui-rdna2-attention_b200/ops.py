@@ -124,6 +124,30 @@ def gemm_i32(a_q, w_q):
     return out
 
 
+def w4a8_scales(scales_fp16):
+    """fp16 group scales [N, K/128] -> the kernel's fp32 [K/128, N] (exact widening, done once per weight)."""
+    return scales_fp16.to(torch.float32).t().contiguous()
+
+
+def gemm_w4a8(a_q, a_scale, w_packed, gscale, bias=None, out=None):
+    """fp16 [M, N] = sum over groups of int32 (a_q . w^T)_g * gscale[g, n], times a_scale[m] (+ bias).
+    w_packed uint8 [N, K/2] (low nibble = even k); gscale fp32 [K/128, N] (see w4a8_scales)."""
+    require_cuda(a_q, a_scale, w_packed, gscale, bias)
+    M, K = a_q.shape
+    N = w_packed.shape[0]
+    if a_q.dtype != torch.int8 or w_packed.dtype != torch.uint8 or w_packed.shape[1] * 2 != K:
+        raise RuntimeError("gemm_w4a8 operands must be int8 [M, K] and packed uint8 [N, K/2]")
+    if gscale.dtype != torch.float32 or gscale.shape != (K // 128, N) or not gscale.is_contiguous():
+        raise RuntimeError("gemm_w4a8 scales must be contiguous fp32 [K/128, N]")
+    if bias is not None and (bias.dtype != torch.float16 or not bias.is_contiguous()):
+        raise RuntimeError("gemm_w4a8 bias must be contiguous fp16")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=a_q.device)
+    call("b2_gemm_w4a8", ptr(a_q.contiguous()), ptr(w_packed.contiguous()), ptr(a_scale), ptr(gscale), ptr(bias),
+         ptr(out), I(M), I(N), I(K), stream())
+    return out
+
+
 def attention(q, k, v, out, scale, int8_qk=False, workspace=None):
     """Fused attention on (B, H, L, 128) fp16 views with a contiguous last dimension; writes ``out``."""
     require_cuda(q, k, v, out)

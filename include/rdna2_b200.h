@@ -91,6 +91,18 @@ int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const float* ws, 
 int b2_gemm_i32(const int8_t* A, const int8_t* B, int32_t* C32, int M, int N, int K, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * W4A8 GEMM with group-128 weight scales (the configuration's tuned-int4 form). The reference's int4 path is
+ * per-channel W4A4 (int8_gemm.hip gemm_i4 :412, quant_row_i4 :62-91; int8_gemm.py wrap_w4a4 :90-103); this entry
+ * point keeps that call's role (packed int4 weights read as stored, row-scaled int8 activations, fp16 out).
+ *   acc_g = int32 dot of A[m, 128g..] and W[n, 128g..]; F = fma(acc_g, gscale[g, n], F) in group order;
+ *   C = fp16(F * as[m] (+ bias[n])).
+ * Wp: uint8 [N, K/2], low nibble = even k, nibbles two's complement in [-8, 7]. gscale: fp32 [K/128, N] (the fp16
+ * group scales, transposed and widened). K % 128 == 0, N % 8 == 0, 16-byte aligned operands.
+ * ------------------------------------------------------------------------------------------------ */
+int b2_gemm_w4a8(const int8_t* A, const uint8_t* Wp, const float* as, const float* gscale, const uint16_t* bias,
+                 uint16_t* C, int M, int N, int K, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Fused attention, head dim 128, no mask. Replaces hip_attention.hip pack_kv + attn (:32,:280) and
  * pack_kv_i8 + attn_i8 (:59,:161), launched from hip_attention.py:48-66 (called by attention.py:46-61).
  * q [B,H,Lq,128], k/v [B,Hkv,Lk,128], out [B,H,Lq,128], fp16, any element strides (b, h, l) that are

@@ -39,8 +39,10 @@ def w4a8_grouped(a_q, a_scale, w_packed, w_scales, group=128, bias=None):
     """W4A8 with per-group int32 accumulation: out = fp16(sum_g (acc_g * sw[n, g]) * sa[m] (+ bias)).
 
     The configuration's grouped form has no reference kernel (the reference's gemm_i4 is per-channel W4A4,
-    int8_gemm.hip:412, int8_gemm.py:90-103), so this is the specification: acc_g = int32 dot over the g-th 128 k,
-    converted to fp32 and scaled by the fp16 group scale, groups summed in order in fp32, then times the row scale.
+    int8_gemm.hip:412, int8_gemm.py:90-103), so this is the specification: acc_g = int32 dot over the g-th 128 k
+    (exact), converted to fp32 (exact, |acc_g| < 2^22), and combined in group order with one fused multiply-add per
+    group, F = fma(acc_g, s[n, g], F) in fp32, then y = F * sa[m] (+ bias) with separate roundings, -> fp16.
+    The fma is evaluated in extended precision (the product is exact there) and rounded once to fp32.
     """
     w = unpack_int4(w_packed)
     K = w.shape[1]
@@ -48,7 +50,8 @@ def w4a8_grouped(a_q, a_scale, w_packed, w_scales, group=128, bias=None):
     out = np.zeros((a_q.shape[0], w.shape[0]), F32)
     for g in range(K // group):
         acc = int_mm(a_q[:, g * group:(g + 1) * group], w[:, g * group:(g + 1) * group])
-        out = out + acc.astype(F32) * sw[None, :, g]
+        prod = acc.astype(np.longdouble) * sw[None, :, g].astype(np.longdouble)
+        out = (prod + out.astype(np.longdouble)).astype(F32)
     y = out * np.asarray(a_scale, F32)[:, None]
     if bias is not None:
         y = y + np.asarray(bias).astype(F32)[None, :]
