@@ -38,6 +38,7 @@ SIGNATURES = {
     "b2_rotate": (I, [P, P, I64, I, P]),
     "b2_gemv_i8": (I, [P, P, P, P, P, I, I, P]),
     "b2_attn_decode": (I, [P, P, P, P, P, P, P, I, I, I, I, F, P]),
+    "b2_attn_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, F, P]),
 }
 
 _lib = None

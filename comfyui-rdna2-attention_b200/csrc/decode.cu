@@ -278,3 +278,74 @@ extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, co
     attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
     return check_launch("attn_merge_kernel");
 }
+
+// ---------------------------------------------------------------- decode attention without allocation
+// Some callers cannot allocate device memory: a host whose device memory is owned by another allocator (a
+// framework's caching pool) and which therefore has no scratch to hand out, or an FFI caller that only holds
+// pointers to its own inputs and outputs. b2_attn_decode_noalloc serves them: the split partials and statistics
+// that b2_attn_decode takes from the caller live here instead, in a file-scope device array of fixed size that every
+// GPU loading this library holds until the process exits.
+#include <mutex>
+
+namespace b2 {
+namespace {
+
+constexpr int NOALLOC_MAX_ROWS = 128;  // batch x query heads
+constexpr size_t NOALLOC_PARTIAL = (size_t)NOALLOC_MAX_ROWS * DEC_SPLITS * HEAD;
+constexpr size_t NOALLOC_STATS = (size_t)NOALLOC_MAX_ROWS * DEC_SPLITS * 2;
+static __device__ __align__(256) float g_decode_scratch[NOALLOC_PARTIAL + NOALLOC_STATS];  // 2.1 MB
+
+// Device address of g_decode_scratch per device. The symbol's name in host code is only a host-side stand-in, so
+// the address comes from cudaGetSymbolAddress, once per device with that device current.
+float* g_scratch_addr[64] = {};
+std::mutex g_scratch_mutex;
+
+int scratch_for_current_device(float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(B2_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return fail(B2_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (e != cudaSuccess) return fail(B2_ERR_CUDA, "cudaGetSymbolAddress(decode scratch): %s", cudaGetErrorString(e));
+        g_scratch_addr[dev] = static_cast<float*>(p);
+    }
+    *out = g_scratch_addr[dev];
+    return B2_OK;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_attn_decode_noalloc(const float* q, const float* k, const float* v, const int32_t* lengths, float* out,
+                                      int batch, int heads, int kv_heads, int capacity, float scale, void* stream) {
+    if (!q || !k || !v || !lengths || !out) return fail(B2_ERR_INVALID, "attn_decode_noalloc: null pointer");
+    if (batch < 0 || heads <= 0 || kv_heads <= 0 || capacity <= 0 || heads % kv_heads)
+        return fail(B2_ERR_INVALID, "attn_decode_noalloc: bad shape");
+    if ((int64_t)batch * heads > NOALLOC_MAX_ROWS)
+        return fail(B2_ERR_UNSUPPORTED, "attn_decode_noalloc: batch x heads = %lld exceeds its fixed scratch of %d rows",
+                    (long long)batch * heads, NOALLOC_MAX_ROWS);
+    const int group = heads / kv_heads;
+    if (group != 1 && group != 2 && group != 4 && group != 8)
+        return fail(B2_ERR_UNSUPPORTED, "attn_decode_noalloc: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
+    if (batch == 0) return B2_OK;
+    float* scratch = nullptr;
+    if (int rc = scratch_for_current_device(&scratch)) return rc;
+    // Every (row, split) slot that attn_merge reads is written by attn_decode first, so the array's previous
+    // contents never leak into a result and nothing needs clearing.
+    float* partial = scratch;
+    float* stats = scratch + NOALLOC_PARTIAL;
+    dim3 grid(DEC_SPLITS, batch * kv_heads);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (group) {
+        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        default: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+    }
+    if (int rc = check_launch("attn_decode_kernel(noalloc)")) return rc;
+    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
+    return check_launch("attn_merge_kernel(noalloc)");
+}

@@ -145,6 +145,15 @@ int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float*
  * scratch from the caller. */
 int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out, float* partial,
                    float* stats, int batch, int heads, int kv_heads, int capacity, float scale, void* stream);
+/* b2_attn_decode without the caller's scratch. It has no counterpart in the reference (whose attention_decode
+ * allocates its partials with torch.empty, int8_gemv.py:108-110). It is for callers that cannot allocate device
+ * memory: hosts whose device memory belongs to another allocator and FFI callers that hold only their own inputs
+ * and outputs. The split partials live in a fixed device array inside this library, 2.1 MB on every GPU that loads
+ * it, for at most batch x heads = 128 query rows; larger calls return B2_ERR_UNSUPPORTED. The first call on a
+ * device looks up that array's address, so make it before any stream capture. All calls share the array: calls that
+ * overlap on the GPU (other streams, other threads) race on it. Nothing in it needs to start at zero. */
+int b2_attn_decode_noalloc(const float* q, const float* k, const float* v, const int32_t* lengths, float* out, int batch,
+                           int heads, int kv_heads, int capacity, float scale, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop
