@@ -402,6 +402,172 @@ class W4A8C3:
         return 2.0 * M * N * K / dt / 1e12, "512 of the 2809 rows through the oracle pre-pass + per-group torch._int_mm + fp32 combine"
 
 
+class GemmQKV(GemmC1):
+    """The C4 QKV projection alone (M = 2 x 3321 tokens, N = 9216, K = 3072): the DiT step's GEMM shape."""
+    name = "gemm_qkv"
+    metric = "W8A8 GEMM TOPS (C4 QKV projection 6642x9216x3072, pre-pass + GEMM)"
+    M, K, N = 6642, 3072, 9216
+    config = {"workload": "C4 QKV projection", "M": 6642, "K": 3072, "N": 9216, "rotation": "block-128 Sylvester",
+              "l2": "rotating input/weight sets > 2x L2"}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        return None, "not measured for this single-kernel case"
+
+
+class PrepassC4:
+    """The C4 QKV pre-pass alone: RMSNorm + block-128 rotation + per-token int8 of [6642, 3072] fp16."""
+    name = "prepass"
+    metric = "pre-pass GB/s (C4: RMSNorm + block-128 Hadamard + int8 of 6642x3072 fp16)"
+    unit = "GB/s"
+    higher = True
+    M, K = 6642, 3072
+
+    def __init__(self, dev):
+        p = pkg()
+        self.ops = p.ops
+        g = torch.Generator().manual_seed(6)
+        self.x_host = torch.randn((self.M, self.K), generator=g).half().pin_memory()
+        self.bytes = self.M * self.K * 2 + self.M * self.K + self.M * 4 + self.K * 4
+        self.sets = max(2, math.ceil(2 * L2_BYTES / self.bytes))
+        self.xs = [self.x_host.to(dev) for _ in range(self.sets)]
+        self.w = (torch.randn(self.K, generator=g) * 0.02).float().to(dev)
+        self.ones = torch.ones((1, self.K), dtype=torch.float16, device=dev)
+        self.zeros = torch.zeros((1, self.K), dtype=torch.float16, device=dev)
+        self.outs = [(torch.empty((self.M, self.K), dtype=torch.int8, device=dev),
+                      torch.empty((self.M,), dtype=torch.float32, device=dev)) for _ in range(self.sets)]
+        self.q_host = torch.empty((self.M, self.K), dtype=torch.int8).pin_memory()
+        self.events = []
+        self.launches_per_step = 1
+        self.config = {"workload": "C4 QKV pre-pass", "M": self.M, "K": self.K, "rotation": "block-128 Sylvester",
+                       "l2": "rotating input sets > 2x L2"}
+
+    def step(self, i, record=False):
+        s = i % self.sets
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.ops.mod_quant_pack_a(self.xs[s], self.w, self.ones, self.zeros, self.M, 1e-6, 128, out=self.outs[s])
+        if record:
+            e1.record()
+            self.events.append((e0, e1))
+
+    def e2e_step(self, i):
+        s = i % self.sets
+        x = self.x_host.to(self.xs[s].device, non_blocking=True)
+        q, _ = self.ops.mod_quant_pack_a(x, self.w, self.ones, self.zeros, self.M, 1e-6, 128)
+        self.q_host.copy_(q, non_blocking=True)
+
+    h2d_bytes = property(lambda self: self.M * self.K * 2)
+    d2h_bytes = property(lambda self: self.M * self.K)
+
+    def value(self, ms, steps, world):
+        return self.bytes * steps * world / (ms * 1e-3) / 1e9
+
+    def roofline(self, peaks, kms):
+        achieved = self.bytes / (kms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "prepass_kernel<MOD,128>",
+                "note": f"{peaks['source']} HBM copy bandwidth"}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        from oracle import quant as oq
+
+        g = np.random.default_rng(6)
+        M, K = 512, PrepassC4.K
+        x = g.standard_normal((M, K)).astype(np.float16)
+        t0 = time.perf_counter()
+        oq.prepass(x, 128, act="mod", w=np.zeros(K, np.float32), s=np.ones((1, K), np.float16),
+                   t=np.zeros((1, K), np.float16), L=M)
+        dt = time.perf_counter() - t0
+        return (M * K * 3 + M * 4) / dt / 1e9, "512 of 6642 rows through the numpy oracle pre-pass"
+
+
+class DecodeC5:
+    name = "decode"
+    metric = "single-token decode ms/token (C5: 36-layer int8 decoder, hidden 2560, 32/8 heads of 128, MLP 9728, KV 1024)"
+    unit = "ms/token"
+    higher = False
+
+    def __init__(self, dev):
+        import importlib
+
+        p = pkg()
+        self.ops = p.ops
+        decoder = importlib.import_module(p.__name__ + ".decoder")
+        self.cfg = cfg = decoder.DecoderConfig()
+        self.dec = decoder.TextDecoder(cfg, dev, seed=0)
+        self.dec.set_position(cfg.capacity - 1)
+        g = torch.Generator().manual_seed(5)
+        self.x_host = torch.randn((1, cfg.hidden), generator=g).pin_memory()
+        self.x0 = self.x_host.to(dev)
+        self.out_host = torch.empty_like(self.x_host).pin_memory()
+        self.dec.x.copy_(self.x0)
+        self.dec.capture()
+        self.bytes, self.weight_bytes = self.dec.bytes_per_token()
+        self.launches_per_step = cfg.layers * decoder.TextDecoder.launches_per_layer
+        self.events = []
+        self.config = {"workload": "C5 single-token decode", "layers": 36, "hidden": 2560, "heads": 32, "kv_heads": 8,
+                       "mlp": 9728, "kv_len": 1024, "batch": 1, "graph": "whole token step in one CUDA graph",
+                       "l2": "3.6 GB of weights per token, larger than L2"}
+
+    def step(self, i, record=False):
+        self.dec.x.copy_(self.x0)
+        if record:
+            # GEMV kernel timing: the gate|up weights of every layer in turn (50 MB each, 1.8 GB together).
+            L = self.dec.layers[i % len(self.dec.layers)]
+            h = torch.randn((self.cfg.hidden,), device=self.x0.device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            self.ops.gemv_i8(h, L.w_gu, L.s_gu)
+            e1.record()
+            self.events.append((e0, e1))
+            self.gemv_bytes = L.w_gu.numel() + L.s_gu.numel() * 4 + h.numel() * 4 + L.w_gu.shape[0] * 4
+        self.dec.graph.replay()
+
+    def e2e_step(self, i):
+        self.dec.x.copy_(self.x_host, non_blocking=True)
+        self.dec.graph.replay()
+        self.out_host.copy_(self.dec.x, non_blocking=True)
+
+    h2d_bytes = property(lambda self: self.cfg.hidden * 4)
+    d2h_bytes = property(lambda self: self.cfg.hidden * 4)
+
+    def value(self, ms, steps, world):
+        return ms / steps
+
+    def roofline(self, peaks, kms):
+        achieved = self.gemv_bytes / (kms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "gemv_i8_kernel (gate|up, 19456 x 2560)",
+                "note": f"{peaks['source']} HBM copy bandwidth; step bytes {self.bytes / 1e9:.3f} GB per token"}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        """The reference's non-GEMV path, F.linear(x, w.to(fp32) * scale) (int8_gemv.py:58-59), and an fp32 softmax
+        decode attention, for 4 of the 36 layers, scaled to 36."""
+        import torch.nn.functional as Fn
+
+        torch.set_num_threads(threads)
+        g = torch.Generator().manual_seed(0)
+        D, F = 2560, 9728
+        shapes = [(6144, D), (D, 4096), (2 * F, D), (D, F)]
+        ws = [(torch.randint(-127, 128, s, generator=g, dtype=torch.int8), torch.rand(s[0], generator=g) * 1e-3) for s in shapes]
+        kc = torch.randn((1024, 8, 128), generator=g)
+        vc = torch.randn((1024, 8, 128), generator=g)
+        x = torch.randn((1, D), generator=g)
+        t0 = time.perf_counter()
+        for _ in range(4):
+            for w, sc in ws:
+                Fn.linear(torch.randn((1, w.shape[1]), generator=g), w.to(torch.float32) * sc[:, None])
+            q = torch.randn((32, 128), generator=g)
+            s_ = torch.einsum("hd,khd->hk", q, kc.repeat_interleave(4, 1)) * 128 ** -0.5
+            torch.softmax(s_, -1) @ vc.repeat_interleave(4, 1).transpose(0, 1)
+        dt = (time.perf_counter() - t0) / 4 * 36
+        return dt * 1e3, "4 of 36 layers through the reference's F.linear(x, w.float() * scale) fallback + fp32 softmax attention, scaled to 36 layers"
+
+
 class KindTimer:
     """Records CUDA events around each launch of a kind ("gemm", "attention", ...) during one instrumented step."""
 
@@ -559,7 +725,7 @@ class DiTC4:
 
 
 WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4,
-             "w4a8": W4A8C3}
+             "w4a8": W4A8C3, "gemm_qkv": GemmQKV, "prepass": PrepassC4, "decode": DecodeC5}
 
 
 def reference_arm(args, world, rank):
@@ -580,6 +746,10 @@ def reference_arm(args, world, rank):
         v, sample = W4A8C3.cpu_baseline(threads)
         metric, unit, higher, cfg = W4A8C3.metric, W4A8C3.unit, True, {"workload": "C3 W4A8 linear", "M": 2809,
                                                                          "K": 3072, "N": 8192, "group": 128}
+    elif name == "decode":
+        v, sample = DecodeC5.cpu_baseline(threads)
+        metric, unit, higher = DecodeC5.metric, DecodeC5.unit, False
+        cfg = {"workload": "C5 single-token decode", "layers": 36, "hidden": 2560, "kv_len": 1024}
     elif name == "dit":
         v, sample = DiTC4.cpu_baseline(threads)
         metric, unit, higher = DiTC4.metric, DiTC4.unit, False

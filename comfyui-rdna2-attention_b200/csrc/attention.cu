@@ -8,13 +8,9 @@
 //     values rint(x/scale) (half-even); s = ((float)int_dot * (qs*c)) * ks; p = exp2(s - m); PV stays fp16.
 // Keys past Lk are masked (score -inf), queries past Lq are not stored.
 //
-// One CTA computes a 128-row Q tile of one (batch, head):
-//   warp 0      TMA: Q once, then K/V tiles of 128 keys into a 2-deep ring (fp16: two 64-column boxes each)
-//   warp 1      TMEM owner and single-thread tcgen05.mma issuer:
-//                 S[j%2] = Q K_j^T   (TMEM, 128 columns each, double-buffered so QK_{j+1} overlaps softmax_j)
-//                 O     += P_j V_j   (TMEM, 128 fp32 columns; V is the MN-major B operand in its natural layout)
-//   warps 2..5  softmax: thread = query row = TMEM lane; reads S, rescales O in TMEM when needed,
-//               writes P (fp16) to shared memory in the 128-byte-swizzled K-major layout, final O / l.
+// One CTA computes two 128-row Q tiles of one (batch, head) with two softmax warpgroups in ping-pong; S, P and O
+// live in TMEM (P overwrites the consumed S columns and is the A operand of the PV MMA). V is the MN-major B operand
+// of the PV MMA in its natural [keys][d] layout. See attention_kernel for the roles.
 #include "common.cuh"
 #include "host.hpp"
 
@@ -23,24 +19,22 @@ namespace {
 
 __device__ unsigned int g_status;
 
-constexpr int TQ = 128;   // query rows per CTA
+constexpr int TQ = 128;   // query rows per tile; a CTA computes two tiles (A and B) of one (batch, head)
 constexpr int TK = 128;   // keys per tile
 constexpr int HD = 128;   // head dim
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_THREADS = 320;
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <bool I8>
 struct AttCfg {
-    static constexpr int Q_BYTES = I8 ? TQ * HD : TQ * HD * 2;
+    static constexpr int Q_BYTES = I8 ? TQ * HD : TQ * HD * 2;  // per tile
     static constexpr int K_BYTES = I8 ? TK * HD : TK * HD * 2;
     static constexpr int V_BYTES = TK * HD * 2;
-    static constexpr int P_BYTES = TQ * TK * 2;
     static constexpr int KS_BYTES = I8 ? TK * 4 : 0;
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-    static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-    static constexpr int OFF_KS = OFF_P + P_BYTES;
+    static constexpr int OFF_KS = OFF_V + 2 * V_BYTES;
     static constexpr int OFF_BAR = OFF_KS + 2 * KS_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
 };
@@ -59,10 +53,15 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-__device__ __forceinline__ void ld32(uint32_t taddr, uint32_t* r) {
-    tmem_ld32_wait(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
-}
-
+// One CTA: 2 x 128 query rows of one (batch, head).
+//   warp 0      TMA: both Q tiles once, then K/V tiles of 128 keys into a 2-deep ring
+//   warp 1      TMEM owner and single-thread tcgen05.mma issuer. TMEM columns: S_A [0,128), S_B [128,256),
+//               O_A [256,384), O_B [384,512). Issue order per key tile j:
+//                 PV_A(j-1) ... S_A(j) ... PV_B(j-1) ... S_B(j)
+//               so the softmax of tile A on S_A(j) overlaps the tensor work for tile B and vice versa.
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B: thread = query row = TMEM lane. Two passes over S
+//               (row max, then p = exp2), P written back as fp16 into the consumed S columns, where the PV MMA
+//               reads it as its A operand (TMEM); lazy, warp-uniform rescale of O in TMEM.
 template <bool I8>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -72,20 +71,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::OFF_BAR);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* k_full = bars + 1;   // [2] stages
     uint64_t* v_full = bars + 3;   // [2]
     uint64_t* k_empty = bars + 5;  // [2]
     uint64_t* v_empty = bars + 7;  // [2]
-    uint64_t* s_full = bars + 9;   // [2]
-    uint64_t* s_free = bars + 11;  // [2]
-    uint64_t* p_full = bars + 13;
-    uint64_t* o_done = bars + 14;
+    uint64_t* s_full = bars + 9;   // [2] tiles A, B
+    uint64_t* p_full = bars + 11;  // [2]
+    uint64_t* o_done = bars + 13;  // [2]
     uint64_t* drain = bars + 15;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q0 = blockIdx.x * TQ;
+    const int q0 = blockIdx.x * (2 * TQ);
     const int bh = blockIdx.y;
     const int b = bh / a.H, h = bh % a.H;
     const int hkv = h / a.rep;
@@ -97,14 +95,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&v_full[i], 1);
-            // int8: the key scales in the K stage are read by the softmax threads too.
-            mbar_init(&k_empty[i], I8 ? 1 + 128 : 1);
+            // int8: the key scales in the K stage are read by both softmax warpgroups too.
+            mbar_init(&k_empty[i], I8 ? 1 + 256 : 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 128);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&o_done[i], 1);
         }
-        mbar_init(p_full, 128);
-        mbar_init(o_done, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -127,19 +124,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     unsigned char* sQ = smem + C_::OFF_Q;
     unsigned char* sK = smem + C_::OFF_K;
     unsigned char* sV = smem + C_::OFF_V;
-    unsigned char* sP = smem + C_::OFF_P;
     float* sKS = reinterpret_cast<float*>(smem + C_::OFF_KS);
 
     if (warp == 0) {
         if (lane == 0) {
             uint32_t k_issued = 0, v_issued = 0, k_ph = 0, v_ph = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(q_full, C_::Q_BYTES);
-            if (I8) {
-                tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
-            } else {
-                tma_load_4d(sQ, &tmQ, q_full, 0, q0, h, b);
-                tma_load_4d(sQ + TQ * 128, &tmQ, q_full, 64, q0, h, b);
+            mbar_arrive_expect_tx(q_full, 2 * C_::Q_BYTES);
+            for (int t = 0; t < 2; ++t) {
+                unsigned char* dst = sQ + t * C_::Q_BYTES;
+                if (I8) {
+                    tma_load_3d(dst, &tmQ, q_full, 0, q0 + t * TQ, bh);
+                } else {
+                    tma_load_4d(dst, &tmQ, q_full, 0, q0 + t * TQ, h, b);
+                    tma_load_4d(dst + TQ * 128, &tmQ, q_full, 64, q0 + t * TQ, h, b);
+                }
             }
             auto load_k = [&](int j) -> bool {
                 const int st = j & 1;
@@ -187,111 +186,113 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_qk = I8 ? idesc_make(2, 1, 0, 0, TQ, TK) : idesc_make(1, 0, 0, 0, TQ, TK);
             constexpr uint32_t idesc_pv = idesc_make(1, 0, 0, 1, TQ, HD);
-            bool ok = mbar_wait(q_full, 0, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA);
             const uint32_t q_addr = smem_u32(sQ);
-            const uint32_t p_addr = smem_u32(sP);
-            for (int j = 0; j <= n_tiles && ok; ++j) {
-                if (j < n_tiles) {
-                    const int st = j & 1, sb = j & 1;
-                    if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
-                    if (j >= 2 && !mbar_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(sK + st * C_::K_BYTES);
-                    const uint32_t d = tmem + sb * TK;
-                    if (I8) {
+            auto issue_s = [&](int t, int j) {
+                const uint32_t k_addr = smem_u32(sK + (j & 1) * C_::K_BYTES);
+                const uint32_t qa = q_addr + t * C_::Q_BYTES;
+                const uint32_t d = tmem + t * TK;
+                if (I8) {
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_i8_ss(d, sdesc_sw128(q_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 32, 16, 1024),
-                                      idesc_qk, kk != 0);
-                    } else {
-#pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const uint32_t off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
-                            mma_f16_ss(d, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-                                       idesc_qk, kk != 0);
-                        }
-                    }
-                    tc_commit(&k_empty[st]);
-                    tc_commit(&s_full[sb]);
-                }
-                if (j >= 1) {
-                    const int jj = j - 1, st = jj & 1;
-                    if (!mbar_wait(p_full, jj & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
-                    if (!mbar_wait(&v_full[st], (jj >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
-                    tc_fence_after();
-                    const uint32_t v_addr = smem_u32(sV + st * C_::V_BYTES);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_i8_ss(d, sdesc_sw128(qa + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 32, 16, 1024), idesc_qk,
+                                  kk != 0);
+                } else {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t a_off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
-                        mma_f16_ss(tmem + 256, sdesc_sw128(p_addr + a_off, 16, 1024),
-                                   sdesc_sw128(v_addr + kk * 2048, TK * 128, 1024), idesc_pv, (jj | kk) != 0);
+                        const uint32_t off = (kk >> 2) * (TQ * 128) + (kk & 3) * 32;
+                        mma_f16_ss(d, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024), idesc_qk,
+                                   kk != 0);
                     }
-                    tc_commit(&v_empty[st]);
-                    tc_commit(o_done);
+                }
+                tc_commit(&s_full[t]);
+            };
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t v_addr = smem_u32(sV + (j & 1) * C_::V_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16_ts(tmem + 256 + t * HD, tmem + t * TK + kk * 8, sdesc_sw128(v_addr + kk * 2048, TK * 128, 1024),
+                               idesc_pv, (j | kk) != 0);
+                tc_commit(&o_done[t]);
+            };
+            bool ok = mbar_wait(q_full, 0, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA) &&
+                      mbar_wait(&k_full[0], 0, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, 0);
+                issue_s(1, 0);
+                tc_commit(&k_empty[0]);
+            }
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int st = j & 1;
+                if (!mbar_wait(&p_full[0], j & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA) ||
+                    !mbar_wait(&v_full[st], (j >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA))
+                    break;
+                tc_fence_after();
+                issue_pv(0, j);
+                const bool more = j + 1 < n_tiles;
+                if (more) {
+                    if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
+                    tc_fence_after();
+                    issue_s(0, j + 1);
+                }
+                if (!mbar_wait(&p_full[1], j & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) break;
+                tc_fence_after();
+                issue_pv(1, j);
+                tc_commit(&v_empty[st]);
+                if (more) {
+                    issue_s(1, j + 1);
+                    tc_commit(&k_empty[(j + 1) & 1]);
                 }
             }
             tc_commit(drain);
             if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
         }
     } else {
-        // Softmax warpgroup: thread -> query row r, TMEM lane r.
+        // Softmax warpgroups: t = 0 (warps 2..5) or 1 (warps 6..9); thread -> query row r of tile t, TMEM lane r.
+        const int t = (warp - 2) >> 2;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        const uint32_t tO = tmem + lane_base + 256;
+        const uint32_t tS = tmem + lane_base + t * TK;
+        const uint32_t tO = tmem + lane_base + 256 + t * HD;
+        const int qrow = q0 + t * TQ + r;
         float m = -1e30f, l = 0.f;
         float qs_c = 0.f;
-        if (I8) {
-            const int qr = min(q0 + r, a.Lq - 1);
-            qs_c = __fmul_rn(a.qscale[(int64_t)bh * a.Lq + qr], a.scale_log2);
-        }
+        if (I8) qs_c = __fmul_rn(a.qscale[(int64_t)bh * a.Lq + min(qrow, a.Lq - 1)], a.scale_log2);
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int sb = j & 1;
-            if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+            if (!mbar_wait(&s_full[t], j & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t sr[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) ld32(tmem + lane_base + sb * TK + c * 32, sr + c * 32);
-            tc_fence_before();
-            mbar_arrive(&s_free[sb]);
-
-            const int valid = a.Lk - j * TK;  // keys of this tile that exist
-            float* x = reinterpret_cast<float*>(sr);  // scores, converted in place
+            const int valid = a.Lk - j * TK;
+            const float* ks = sKS + (j & 1) * TK;
+            // Pass 1: row max of the scores (log2 domain).
             float mx = -1e30f;
-            if (I8) {
-                const float* ks = sKS + (j & 1) * TK;
 #pragma unroll
-                for (int i = 0; i < 128; ++i) {
-                    const float v = __fmul_rn(__fmul_rn((float)(int32_t)sr[i], qs_c), ks[i]);
-                    x[i] = i < valid ? v : -1e30f;
-                    mx = fmaxf(mx, x[i]);
-                }
-                // Key scales of this stage are consumed.
-                mbar_arrive(&k_empty[j & 1]);
-            } else {
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[32];
+                tmem_ld32_wait(tS + c * 32, v);
 #pragma unroll
-                for (int i = 0; i < 128; ++i) {
-                    x[i] = i < valid ? __uint_as_float(sr[i]) : -1e30f;
-                    mx = fmaxf(mx, x[i]);
+                for (int i = 0; i < 32; ++i) {
+                    const int col = c * 32 + i;
+                    const float x = I8 ? __fmul_rn(__fmul_rn((float)(int32_t)v[i], qs_c), ks[col]) : __uint_as_float(v[i]);
+                    if (valid >= TK || col < valid) mx = fmaxf(mx, x);
                 }
-                mx *= a.scale_log2;
             }
-            bool o_ready = false;
+            if (!I8) mx *= a.scale_log2;
             if (__any_sync(0xffffffffu, mx > m + 8.f)) {
                 const float mn = fmaxf(m, mx);
                 const float alpha = ex2(m - mn);
                 m = mn;
                 l *= alpha;
                 if (j > 0) {
-                    if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                    // O holds PV of the previous tiles; it must be complete before it is rescaled.
+                    if (!mbar_wait(&o_done[t], (j - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
                         ok = false;
                         break;
                     }
-                    o_ready = true;
                     tc_fence_after();
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
@@ -301,48 +302,43 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                         tmem_st32(tO + c * 32, o);
                     }
-                    tmem_wait_st();
                 }
             }
-            // p = exp2(s*c - m), fp16 for PV; l sums the fp32 values.
-            uint32_t ph[64];
+            // Pass 2: p = exp2(s*c - m) (fp16 path) or exp2(s - m) (int8), l sums the fp32 p, P (fp16 pairs) goes
+            // into the columns of S already consumed: chunk c of 32 scores -> columns [16c, 16c + 16).
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                float p0, p1;
-                if (I8) {
-                    p0 = ex2(x[2 * i] - m);
-                    p1 = ex2(x[2 * i + 1] - m);
-                } else {
-                    p0 = ex2(fmaf(x[2 * i], a.scale_log2, -m));
-                    p1 = ex2(fmaf(x[2 * i + 1], a.scale_log2, -m));
-                }
-                l += p0 + p1;
-                const __half2 hp = __floats2half2_rn(p0, p1);
-                ph[i] = *reinterpret_cast<const uint32_t*>(&hp);
-            }
-            if (j > 0 && !o_ready) {
-                // P of the previous tile is still being read by its PV MMA.
-                if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
-                    ok = false;
-                    break;
-                }
-            }
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[32], pk[16];
+                tmem_ld32_wait(tS + c * 32, v);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                unsigned char* atom = sP + (c >> 3) * (TQ * 128);
-                const int chunk = (c & 7) ^ (r & 7);
-                *reinterpret_cast<uint4*>(atom + r * 128 + chunk * 16) =
-                    make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+                for (int i = 0; i < 16; ++i) {
+                    float p2[2];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int col = c * 32 + 2 * i + e;
+                        const uint32_t raw = v[2 * i + e];
+                        float p;
+                        if (I8) p = ex2(__fmul_rn(__fmul_rn((float)(int32_t)raw, qs_c), ks[col]) - m);
+                        else p = ex2(fmaf(__uint_as_float(raw), a.scale_log2, -m));
+                        if (valid < TK && col >= valid) p = 0.f;
+                        p2[e] = p;
+                    }
+                    l += p2[0] + p2[1];
+                    const __half2 hp = __floats2half2_rn(p2[0], p2[1]);
+                    pk[i] = *reinterpret_cast<const uint32_t*>(&hp);
+                }
+                tmem_st16(tS + c * 16, pk);
             }
-            fence_proxy_async_smem();
+            if (I8) mbar_arrive(&k_empty[j & 1]);  // key scales of this stage are consumed
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[t]);
         }
-        if (ok && mbar_wait(o_done, (n_tiles - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+        if (ok && mbar_wait(&o_done[t], (n_tiles - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
             tc_fence_after();
             const float inv = 1.f / l;
-            const bool row_ok = q0 + r < a.Lq;
-            __half* dst = a.out + (int64_t)b * a.sob + (int64_t)h * a.soh + (int64_t)(q0 + r) * a.sol;
+            const bool row_ok = qrow < a.Lq;
+            __half* dst = a.out + (int64_t)b * a.sob + (int64_t)h * a.soh + (int64_t)qrow * a.sol;
 #pragma unroll 1
             for (int c = 0; c < 4; ++c) {
                 uint32_t o[32];
@@ -462,7 +458,7 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
         if (int rc = set_smem(attention_kernel<I8>, AttCfg<I8>::SMEM)) return rc;
         configured[dev] = true;
     }
-    dim3 grid((a.Lq + TQ - 1) / TQ, B * a.H);
+    dim3 grid((a.Lq + 2 * TQ - 1) / (2 * TQ), B * a.H);
     attention_kernel<I8><<<grid, ATT_THREADS, AttCfg<I8>::SMEM, s>>>(tq, tk, tv, tks, a);
     return check_launch("attention_kernel");
 }

@@ -96,6 +96,20 @@ __device__ __forceinline__ void load16(const __half* p, float (&f)[16]) {
     }
 }
 
+__device__ __forceinline__ void unpack16(const uint4 (&r)[2], float (&f)[16]) {
+    const __half2* a = reinterpret_cast<const __half2*>(&r[0]);
+    const __half2* b = reinterpret_cast<const __half2*>(&r[1]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 x = __half22float2(a[i]);
+        const float2 y = __half22float2(b[i]);
+        f[2 * i] = x.x;
+        f[2 * i + 1] = x.y;
+        f[8 + 2 * i] = y.x;
+        f[8 + 2 * i + 1] = y.y;
+    }
+}
+
 __device__ __forceinline__ void store16(__half* p, const float (&f)[16]) {
     uint4 lo, hi;
     __half2* a = reinterpret_cast<__half2*>(&lo);
@@ -109,12 +123,15 @@ __device__ __forceinline__ void store16(__half* p, const float (&f)[16]) {
     reinterpret_cast<uint4*>(p)[1] = hi;
 }
 
+// The exponential and the quotient use the hardware approximations (ex2-based __expf, rcp-based __fdividef, a few
+// fp32 ulps); after the fp16 rounding of each stage the activation equals the exact formula's except for about one
+// value in a thousand, by one fp16 step.
 __device__ __forceinline__ float silu_mul(float g, float u) {
-    const float silu = round_h(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
+    const float silu = round_h(__fdividef(g, __fadd_rn(1.f, __expf(-g))));
     return round_h(__fmul_rn(silu, u));
 }
 __device__ __forceinline__ float sigmoid_gate(float x, float g) {
-    const float sig = round_h(__fdiv_rn(1.f, __fadd_rn(1.f, expf(-g))));
+    const float sig = round_h(__fdividef(1.f, __fadd_rn(1.f, __expf(-g))));
     return round_h(__fmul_rn(x, sig));
 }
 __device__ __forceinline__ float modulate(float x, float rstd, float w, float s, float t) {
@@ -122,13 +139,34 @@ __device__ __forceinline__ float modulate(float x, float rstd, float w, float s,
     return round_h(__fadd_rn(round_h(__fmul_rn(n, s)), t));
 }
 
-__device__ __forceinline__ int quant1(float f, float scale) {
-    const float r = floorf(__fadd_rn(__fdiv_rn(f, scale), 0.5f));
-    return (int)fminf(fmaxf(r, -128.f), 127.f);
+// y = fp16(v * c) (a power of two or 1/sqrt(128), one fp32 rounding then one fp16 rounding), parked as 16 fp16 at p;
+// mx2 accumulates max |y| exactly in fp16.
+__device__ __forceinline__ void park16(__half* p, const float (&v)[16], float c, __half2& mx2) {
+    uint4 o[2];
+    __half2* h = reinterpret_cast<__half2*>(o);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        h[i] = __floats2half2_rn(__fmul_rn(v[2 * i], c), __fmul_rn(v[2 * i + 1], c));
+        mx2 = __hmax2(mx2, __habs2(h[i]));
+    }
+    reinterpret_cast<uint4*>(p)[0] = o[0];
+    reinterpret_cast<uint4*>(p)[1] = o[1];
+}
+
+// floor(f / scale + 0.5) with the IEEE quotient, computed as f * (1/scale): |f / scale| <= 127 keeps that product
+// within 2e-5 of the quotient, so unless f * inv + 0.5 lands within 1e-4 of an integer the floor is the same; those
+// few values take the IEEE divide. The result is bit-identical to floorf(f / scale + 0.5f).
+__device__ __forceinline__ int quant1(float f, float scale, float inv) {
+    const float u = __fmaf_rn(f, inv, 0.5f);
+    float r = floorf(u);
+    if (fabsf(__fsub_rn(__fsub_rn(u, r), 0.5f)) > 0.4999f) r = floorf(__fadd_rn(__fdiv_rn(f, scale), 0.5f));
+    r = fminf(fmaxf(r, -128.f), 127.f);
+    // r is an integer in [-128, 127]: adding 1.5 * 2^23 puts it in the low mantissa bits (exact).
+    return __float_as_int(__fadd_rn(r, 12582912.f)) - 0x4B400000;
 }
 
 template <int ACT, int ROT>
-__global__ void __launch_bounds__(PP_WARPS * 32) prepass_kernel(const PrepassArgs a) {
+__global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const PrepassArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * PP_WARPS + warp;
@@ -147,15 +185,22 @@ __global__ void __launch_bounds__(PP_WARPS * 32) prepass_kernel(const PrepassArg
     if (ACT == ACT_MOD) {
         // Stage the raw row and sum its squares (the norm needs the whole row before any output).
         float ss = 0.f;
-        for (int k0 = lane * 8; k0 < K; k0 += 256) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xptr(k0)));
-            *reinterpret_cast<uint4*>(rowbuf + k0) = raw;
-            const __half2* h = reinterpret_cast<const __half2*>(&raw);
+        for (int c0 = lane * 8; c0 < K; c0 += 8 * 256) {
+            uint4 raw[8];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float2 f = __half22float2(h[i]);
-                ss = fmaf(f.x, f.x, ss);
-                ss = fmaf(f.y, f.y, ss);
+            for (int j = 0; j < 8; ++j)
+                if (c0 + j * 256 < K) raw[j] = __ldg(reinterpret_cast<const uint4*>(xptr(c0 + j * 256)));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (c0 + j * 256 >= K) break;
+                *reinterpret_cast<uint4*>(rowbuf + c0 + j * 256) = raw[j];
+                const __half2* h = reinterpret_cast<const __half2*>(&raw[j]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 f = __half22float2(h[i]);
+                    ss = fmaf(f.x, f.x, ss);
+                    ss = fmaf(f.y, f.y, ss);
+                }
             }
         }
 #pragma unroll
@@ -168,43 +213,70 @@ __global__ void __launch_bounds__(PP_WARPS * 32) prepass_kernel(const PrepassArg
     const __half* srow = ACT == ACT_MOD ? a.s + (int64_t)(row / a.L) * K : nullptr;
     const __half* trow = ACT == ACT_MOD ? a.t + (int64_t)(row / a.L) * K : nullptr;
 
-    float mx = 0.f;
+    __half2 mx2 = __float2half2_rn(0.f);  // running max of |y| over this lane's values (fp16, exact)
     const int npass = (K + 511) >> 9;
-    for (int p = 0; p < npass; ++p) {
+    // Loads for PF passes are issued together, so each warp keeps PF KB (x2 with a second input) in flight.
+    constexpr bool TWO = ACT == ACT_SWIGLU || ACT == ACT_GATE;
+    constexpr int PF = ACT == ACT_MOD ? 1 : (TWO ? 2 : 4);
+    for (int p0 = 0; p0 < npass; p0 += PF) {
+    uint4 rx[PF][2], ru[PF][2];
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+        const int kk = (p0 + j) * 512 + lane * 16;
+        if (ACT != ACT_MOD && p0 + j < npass && kk < K) {
+            const uint4* px = reinterpret_cast<const uint4*>(xptr(kk));
+            rx[j][0] = __ldg(px);
+            rx[j][1] = __ldg(px + 1);
+            if (TWO) {
+                const uint4* pu = reinterpret_cast<const uint4*>(ur + kk);
+                ru[j][0] = __ldg(pu);
+                ru[j][1] = __ldg(pu + 1);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+        const int p = p0 + j;
+        if (p >= npass) break;
         const int k0 = p * 512 + lane * 16;
         const bool active = k0 < K;
         float v[16];
         if (active) {
             if (ACT == ACT_MOD) {
-                float x[16], s[16], t[16];
-                const uint4 r0 = *reinterpret_cast<const uint4*>(rowbuf + k0);
-                const uint4 r1 = *reinterpret_cast<const uint4*>(rowbuf + k0 + 8);
-                const __half2* h0 = reinterpret_cast<const __half2*>(&r0);
-                const __half2* h1 = reinterpret_cast<const __half2*>(&r1);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float2 f0 = __half22float2(h0[i]), f1 = __half22float2(h1[i]);
-                    x[2 * i] = f0.x;
-                    x[2 * i + 1] = f0.y;
-                    x[8 + 2 * i] = f1.x;
-                    x[8 + 2 * i + 1] = f1.y;
-                }
-                load16(srow + k0, s);
-                load16(trow + k0, t);
+                // n = fp16(x * rstd * (w + 1)) in fp32; then fp16(fp16(n * s) + t) as fp16 pairs: the product of two
+                // fp16 values is exact before its single rounding, and a sum of two fp16 values rounded once to
+                // fp16 equals the fp32 sum rounded to fp16, so the packed ops round exactly like the fp32 path.
+                uint4 xr[2], sr[2], tr[2];
+                xr[0] = *reinterpret_cast<const uint4*>(rowbuf + k0);
+                xr[1] = *reinterpret_cast<const uint4*>(rowbuf + k0 + 8);
+                sr[0] = __ldg(reinterpret_cast<const uint4*>(srow + k0));
+                sr[1] = __ldg(reinterpret_cast<const uint4*>(srow + k0) + 1);
+                tr[0] = __ldg(reinterpret_cast<const uint4*>(trow + k0));
+                tr[1] = __ldg(reinterpret_cast<const uint4*>(trow + k0) + 1);
+                const __half2* x2 = reinterpret_cast<const __half2*>(xr);
+                const __half2* s2 = reinterpret_cast<const __half2*>(sr);
+                const __half2* t2 = reinterpret_cast<const __half2*>(tr);
                 const float4* wp = reinterpret_cast<const float4*>(a.w + k0);
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     const float4 w4 = __ldg(wp + i);
-                    v[4 * i + 0] = modulate(x[4 * i + 0], rstd, w4.x, s[4 * i + 0], t[4 * i + 0]);
-                    v[4 * i + 1] = modulate(x[4 * i + 1], rstd, w4.y, s[4 * i + 1], t[4 * i + 1]);
-                    v[4 * i + 2] = modulate(x[4 * i + 2], rstd, w4.z, s[4 * i + 2], t[4 * i + 2]);
-                    v[4 * i + 3] = modulate(x[4 * i + 3], rstd, w4.w, s[4 * i + 3], t[4 * i + 3]);
+                    const float2 xa = __half22float2(x2[2 * i]), xb = __half22float2(x2[2 * i + 1]);
+                    const __half2 na = __floats2half2_rn(__fmul_rn(__fmul_rn(xa.x, rstd), __fadd_rn(w4.x, 1.f)),
+                                                         __fmul_rn(__fmul_rn(xa.y, rstd), __fadd_rn(w4.y, 1.f)));
+                    const __half2 nb = __floats2half2_rn(__fmul_rn(__fmul_rn(xb.x, rstd), __fadd_rn(w4.z, 1.f)),
+                                                         __fmul_rn(__fmul_rn(xb.y, rstd), __fadd_rn(w4.w, 1.f)));
+                    const float2 ya = __half22float2(__hadd2_rn(__hmul2_rn(na, s2[2 * i]), t2[2 * i]));
+                    const float2 yb = __half22float2(__hadd2_rn(__hmul2_rn(nb, s2[2 * i + 1]), t2[2 * i + 1]));
+                    v[4 * i + 0] = ya.x;
+                    v[4 * i + 1] = ya.y;
+                    v[4 * i + 2] = yb.x;
+                    v[4 * i + 3] = yb.y;
                 }
             } else {
-                load16(xptr(k0), v);
-                if (ACT == ACT_SWIGLU || ACT == ACT_GATE) {
+                unpack16(rx[j], v);
+                if (TWO) {
                     float u[16];
-                    load16(ur + k0, u);
+                    unpack16(ru[j], u);
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = ACT == ACT_SWIGLU ? silu_mul(v[i], u[i]) : sigmoid_gate(v[i], u[i]);
                 }
@@ -213,11 +285,7 @@ __global__ void __launch_bounds__(PP_WARPS * 32) prepass_kernel(const PrepassArg
         }
 
         if (ROT == 0) {
-            if (active) {
-#pragma unroll
-                for (int i = 0; i < 16; i++) mx = fmaxf(mx, fabsf(v[i]));
-                store16(rowbuf + k0, v);
-            }
+            if (active) park16(rowbuf + k0, v, 1.f, mx2);
         } else {
             if (active) {
                 if (ROT == 256) {
@@ -241,12 +309,8 @@ __global__ void __launch_bounds__(PP_WARPS * 32) prepass_kernel(const PrepassArg
 #pragma unroll
                     for (int i = 0; i < 16; i++) v[i] = T[tidx<ROT>(16 * hw + i, c)];
                     h16(v);
-#pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const __half y = __float2half_rn(__fmul_rn(v[i], 0.0625f));
-                        rowbuf[p * 512 + (16 * hw + i) * 16 + c] = y;
-                        mx = fmaxf(mx, fabsf(__half2float(y)));
-                    }
+                    // Parked in this lane's own slot (conflict-free); the quant phase knows the positions.
+                    park16(rowbuf + k0, v, 0.0625f, mx2);
                 }
             } else {
                 const int q = lane >> 3, sub = lane & 7;
@@ -262,42 +326,76 @@ __global__ void __launch_bounds__(PP_WARPS * 32) prepass_kernel(const PrepassArg
 #pragma unroll
                         for (int i = 0; i < 16; i++)
                             if ((i & st) == 0) bfly(v[i], v[i + st]);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const __half y0 = __float2half_rn(__fmul_rn(v[2 * j], INV_SQRT128));
-                        const __half y1 = __float2half_rn(__fmul_rn(v[2 * j + 1], INV_SQRT128));
-                        *reinterpret_cast<__half2*>(rowbuf + p * 512 + (8 * q + j) * 16 + 2 * sub) = __halves2half2(y0, y1);
-                        mx = fmaxf(mx, fmaxf(fabsf(__half2float(y0)), fabsf(__half2float(y1))));
-                    }
+                    park16(rowbuf + k0, v, INV_SQRT128, mx2);
                 }
             }
             __syncwarp();
         }
     }
+    }
 
+    float mx = fmaxf(__low2float(mx2), __high2float(mx2));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const float scale = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
+    const float inv = __frcp_rn(scale);
     if (lane == 0) a.scale[row] = scale;
     __syncwarp();
 
+    // Each lane quantizes the 16 values it parked per pass. With a rotation they sit at transposed positions, so
+    // the bytes go through a small shared-memory transpose (the float buffer, now free) and every lane then stores
+    // 16 contiguous bytes: the warp writes 512 contiguous bytes per pass.
     int8_t* qr = a.q + (int64_t)row * K;
-    for (int k0 = lane * 16; k0 < K; k0 += 512) {
-        const uint4 r0 = *reinterpret_cast<const uint4*>(rowbuf + k0);
-        const uint4 r1 = *reinterpret_cast<const uint4*>(rowbuf + k0 + 8);
-        const __half2* h0 = reinterpret_cast<const __half2*>(&r0);
-        const __half2* h1 = reinterpret_cast<const __half2*>(&r1);
-        uint32_t w[4];
+    unsigned char* T8 = reinterpret_cast<unsigned char*>(T);
+    for (int p = 0; p < npass; ++p) {
+        const int k0 = p * 512 + lane * 16;
+        const bool active = k0 < K;
+        uint32_t w[4] = {0, 0, 0, 0};
+        if (active) {
+            const uint4 r0 = *reinterpret_cast<const uint4*>(rowbuf + k0);
+            const uint4 r1 = *reinterpret_cast<const uint4*>(rowbuf + k0 + 8);
+            const __half2* h0 = reinterpret_cast<const __half2*>(&r0);
+            const __half2* h1 = reinterpret_cast<const __half2*>(&r1);
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const float2 a0 = __half22float2(h0[2 * i]), a1 = __half22float2(h0[2 * i + 1]);
-            const float2 b0 = __half22float2(h1[2 * i]), b1 = __half22float2(h1[2 * i + 1]);
-            w[i] = (uint32_t)(quant1(a0.x, scale) & 255) | ((uint32_t)(quant1(a0.y, scale) & 255) << 8) |
-                   ((uint32_t)(quant1(a1.x, scale) & 255) << 16) | ((uint32_t)(quant1(a1.y, scale) & 255) << 24);
-            w[2 + i] = (uint32_t)(quant1(b0.x, scale) & 255) | ((uint32_t)(quant1(b0.y, scale) & 255) << 8) |
-                       ((uint32_t)(quant1(b1.x, scale) & 255) << 16) | ((uint32_t)(quant1(b1.y, scale) & 255) << 24);
+            for (int i = 0; i < 2; i++) {
+                const float2 a0 = __half22float2(h0[2 * i]), a1 = __half22float2(h0[2 * i + 1]);
+                const float2 b0 = __half22float2(h1[2 * i]), b1 = __half22float2(h1[2 * i + 1]);
+                w[i] = (uint32_t)(quant1(a0.x, scale, inv) & 255) | ((uint32_t)(quant1(a0.y, scale, inv) & 255) << 8) |
+                       ((uint32_t)(quant1(a1.x, scale, inv) & 255) << 16) | ((uint32_t)(quant1(a1.y, scale, inv) & 255) << 24);
+                w[2 + i] = (uint32_t)(quant1(b0.x, scale, inv) & 255) | ((uint32_t)(quant1(b0.y, scale, inv) & 255) << 8) |
+                           ((uint32_t)(quant1(b1.x, scale, inv) & 255) << 16) | ((uint32_t)(quant1(b1.y, scale, inv) & 255) << 24);
+            }
         }
-        *reinterpret_cast<uint4*>(qr + k0) = make_uint4(w[0], w[1], w[2], w[3]);
+        if (ROT == 0) {
+            if (active) *reinterpret_cast<uint4*>(qr + k0) = make_uint4(w[0], w[1], w[2], w[3]);
+            continue;
+        }
+        if (active) {
+            if (ROT == 256) {
+                // value i of lane (hw, c) belongs to row 16 hw + i, column c of the pass's 32 x 16 byte block
+                const int hw = lane >> 4, c = lane & 15;
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int r = 16 * hw + i;
+                    T8[r * 16 + (r >> 4) * 16 + c] = (unsigned char)(w[i >> 2] >> (8 * (i & 3)));
+                }
+            } else {
+                // values 2j, 2j+1 of lane (q, sub) belong to row 8 q + j, columns 2 sub, 2 sub + 1
+                const int q = lane >> 3, sub = lane & 7;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int r = 8 * q + j;
+                    *reinterpret_cast<uint16_t*>(T8 + r * 16 + (r >> 3) * 16 + 2 * sub) =
+                        (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+                }
+            }
+        }
+        __syncwarp();
+        if (active) {
+            const int pad = ROT == 256 ? (lane >> 4) * 16 : (lane >> 3) * 16;
+            *reinterpret_cast<uint4*>(qr + k0) = *reinterpret_cast<const uint4*>(T8 + lane * 16 + pad);
+        }
+        __syncwarp();
     }
 }
 
