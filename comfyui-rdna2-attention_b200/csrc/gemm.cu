@@ -46,6 +46,65 @@ struct GemmArgs {
     int M, N, K;
 };
 
+// 32 accumulator columns of one row: dequant (+ bias) (+ residual) -> fp16, or raw int32.
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t taddr, int m, bool row_ok, float sa, int nb) {
+    uint32_t r[32];
+    tmem_ld32_wait(taddr, r);
+    if (!row_ok || nb >= g.N) return;
+    if (g.C32) {
+        int32_t* dst = g.C32 + (int64_t)m * g.N + nb;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (nb + 4 * j < g.N)
+                *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+        return;
+    }
+    __half* dst = g.C + (int64_t)m * g.N + nb;
+    const __half* res = g.R ? g.R + (int64_t)m * g.N + nb : nullptr;
+    const __half* gate = g.R ? g.G + (int64_t)(m / g.L) * g.N + nb : nullptr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (nb + 8 * j >= g.N) break;
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j) + 1);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (g.bias) {
+            const uint4 braw = __ldg(reinterpret_cast<const uint4*>(g.bias + nb + 8 * j));
+            const __half2* bh = reinterpret_cast<const __half2*>(&braw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(bh[e]);
+                bv[2 * e] = f.x;
+                bv[2 * e + 1] = f.y;
+            }
+        }
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float v = __fmul_rn(__fmul_rn((float)(int32_t)r[8 * j + e], sa), wv[e]);
+            y[e] = round_h(g.bias ? __fadd_rn(v, bv[e]) : v);
+        }
+        if (res) {
+            const uint4 rraw = *reinterpret_cast<const uint4*>(res + 8 * j);
+            const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gate + 8 * j));
+            const __half2* rh = reinterpret_cast<const __half2*>(&rraw);
+            const __half2* gh = reinterpret_cast<const __half2*>(&graw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 rf = __half22float2(rh[e]), gf = __half22float2(gh[e]);
+                y[2 * e] = round_h(__fadd_rn(rf.x, round_h(__fmul_rn(gf.x, y[2 * e]))));
+                y[2 * e + 1] = round_h(__fadd_rn(rf.y, round_h(__fmul_rn(gf.y, y[2 * e + 1]))));
+            }
+        }
+        uint4 o;
+        __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
+        *reinterpret_cast<uint4*>(dst + 8 * j) = o;
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
@@ -184,64 +243,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const float sa = (row_ok && g.as) ? g.as[m] : 0.f;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32_wait(taddr + c * 32, r);
-                const int nb = n0 + c * 32;
-                if (!row_ok || nb >= g.N) continue;
-                if (g.C32) {
-                    int32_t* dst = g.C32 + (int64_t)m * g.N + nb;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (nb + 4 * j < g.N)
-                            *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-                    continue;
-                }
-                __half* dst = g.C + (int64_t)m * g.N + nb;
-                const __half* res = g.R ? g.R + (int64_t)m * g.N + nb : nullptr;
-                const __half* gate = g.R ? g.G + (int64_t)(m / g.L) * g.N + nb : nullptr;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (nb + 8 * j >= g.N) break;
-                    const float4 w0 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j));
-                    const float4 w1 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j) + 1);
-                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    if (g.bias) {
-                        const uint4 braw = __ldg(reinterpret_cast<const uint4*>(g.bias + nb + 8 * j));
-                        const __half2* bh = reinterpret_cast<const __half2*>(&braw);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 f = __half22float2(bh[e]);
-                            bv[2 * e] = f.x;
-                            bv[2 * e + 1] = f.y;
-                        }
-                    }
-                    float y[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float v = __fmul_rn(__fmul_rn((float)(int32_t)r[8 * j + e], sa), wv[e]);
-                        y[e] = round_h(g.bias ? __fadd_rn(v, bv[e]) : v);
-                    }
-                    if (res) {
-                        const uint4 rraw = *reinterpret_cast<const uint4*>(res + 8 * j);
-                        const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gate + 8 * j));
-                        const __half2* rh = reinterpret_cast<const __half2*>(&rraw);
-                        const __half2* gh = reinterpret_cast<const __half2*>(&graw);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 rf = __half22float2(rh[e]), gf = __half22float2(gh[e]);
-                            y[2 * e] = round_h(__fadd_rn(rf.x, round_h(__fmul_rn(gf.x, y[2 * e]))));
-                            y[2 * e + 1] = round_h(__fadd_rn(rf.y, round_h(__fmul_rn(gf.y, y[2 * e + 1]))));
-                        }
-                    }
-                    uint4 o;
-                    __half2* oh = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
-                    *reinterpret_cast<uint4*>(dst + 8 * j) = o;
-                }
-            }
+            for (int c = 0; c < BN / 32; ++c) epilogue_chunk(g, taddr + c * 32, m, row_ok, sa, n0 + c * 32);
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
         }
@@ -251,6 +253,195 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, C_::TMEM_COLS);
+}
+
+
+// ---------------------------------------------------------------- CTA-pair kernel
+// Two CTAs of a cluster compute a 256 x 256 tile with cta_group::2 MMAs (M = 256, N = 256, K = 32): CTA r loads rows
+// [128 r, 128 r + 128) of the A tile and of the B tile, the MMA issued by CTA 0 reads both CTAs' shared memory and
+// writes each CTA's 128 accumulator rows x 256 columns into its own TMEM. Per SM this halves the B tile in shared
+// memory (32 KB per k-block instead of 48 KB) for the same tensor work. Completion crosses the pair as ordinary
+// barrier arrivals: TMA of both CTAs completes on CTA 0's full barrier, CTA 0's MMA commits to both CTAs' empty and
+// tfull barriers, and both epilogues arrive on CTA 0's tempty barrier.
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_HALF = 128 * BK;                    // 16 KB: 128 rows x 128 bytes
+constexpr int PAIR_STAGE_BYTES = 2 * PAIR_HALF;        // A half + B half
+constexpr int PAIR_SMEM = PAIR_STAGES * PAIR_STAGE_BYTES + 256 + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PAIR_STAGES * PAIR_STAGE_BYTES);
+    uint64_t* full = bars;                      // [STAGES] (CTA 0)
+    uint64_t* empty = bars + PAIR_STAGES;       // [STAGES] (each CTA)
+    uint64_t* tfull = bars + 2 * PAIR_STAGES;   // [2] (each CTA)
+    uint64_t* tempty = tfull + 2;               // [2] (CTA 0)
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    const int num_m = (g.M + 255) / 256, num_n = (g.N + 255) / 256;
+    const int num_tiles = num_m * num_n;
+    const int KB = (g.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PAIR_STAGES; ++s) {
+            mbar_init(&full[s], 2);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 8);  // one arrival per epilogue warp of each CTA
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // Weights are re-read by every row tile and activations by every column tile: both stay in L2
+            // (evict_last for the weights, the default for the activations).
+            const uint64_t keep = l2_policy_evict_last(), normal = l2_policy_evict_normal();
+            const uint32_t full0 = map_to_rank(smem_u32(full), 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = cluster; tile < num_tiles; tile += nclusters) {
+                const int m0 = (tile % num_m) * 256, n0 = (tile / num_m) * 256;
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, &g_status, B2_DEV_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = smem + stage * PAIR_STAGE_BYTES;
+                    const uint32_t bar = full0 + stage * 8;
+                    mbar_arrive_expect_tx_remote(bar, PAIR_STAGE_BYTES);
+                    tma_load_2d_pair(st, &tmA, bar, kb * BK, m0 + 128 * rank, normal);
+                    tma_load_2d_pair(st + PAIR_HALF, &tmB, bar, kb * BK, n0 + 128 * rank, keep);
+                    if (++stage == PAIR_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_make(2, 1, 0, 0, 256, 256);
+            const uint32_t empty_own = smem_u32(empty), empty_peer = map_to_rank(smem_u32(empty), 1);
+            const uint32_t tfull_own = smem_u32(tfull), tfull_peer = map_to_rank(smem_u32(tfull), 1);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;
+            for (int tile = cluster; tile < num_tiles && ok; tile += nclusters, ++it) {
+                const int acc = it & 1;
+                const uint32_t acc_phase = (it >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * 256;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * PAIR_STAGE_BYTES);
+                    const uint64_t a_desc = sdesc_sw128(a_addr, 16, 1024);
+                    const uint64_t b_desc = sdesc_sw128(a_addr + PAIR_HALF, 16, 1024);
+#pragma unroll
+                    for (int k = 0; k < BK / 32; ++k)
+                        mma_i8_ss_pair(d_tmem, a_desc + (uint64_t)(k * 2), b_desc + (uint64_t)(k * 2), idesc, (kb | k) != 0);
+                    tc_commit_pair(empty_own + stage * 8);
+                    tc_commit_pair(empty_peer + stage * 8);
+                    if (++stage == PAIR_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair(tfull_own + acc * 8);
+                tc_commit_pair(tfull_peer + acc * 8);
+            }
+            tc_commit_pair(smem_u32(drain));
+            if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+        }
+    } else {
+        const int quarter = warp & 3;
+        const int row_local = quarter * 32 + lane;
+        const uint32_t tempty0 = map_to_rank(smem_u32(tempty), 0);
+        int it = 0;
+        for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+            const int acc = it & 1;
+            const uint32_t acc_phase = (it >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
+            tc_fence_after();
+            const int m0 = (tile % num_m) * 256, n0 = (tile / num_m) * 256;
+            const int m = m0 + 128 * rank + row_local;
+            const bool row_ok = m < g.M;
+            const float sa = (row_ok && g.as) ? g.as[m] : 0.f;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) epilogue_chunk(g, taddr + c * 32, m, row_ok, sa, n0 + c * 32);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(tempty0 + acc * 8);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the peer's shared memory and barriers stay alive until the pair is done with them
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
+}
+
+int launch_pair(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_t stream) {
+    CUtensorMap ta, tb;
+    if (int rc = make_map_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.M, g.K, BK, 128)) return rc;
+    if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.K, BK, 128)) return rc;
+    static int clusters[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !clusters[dev]) {
+        if (int rc = set_smem(gemm_w8a8_pair_kernel, PAIR_SMEM)) return rc;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+        cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = PAIR_SMEM;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_w8a8_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sm_count() / 2;
+        }
+        clusters[dev] = n;
+    }
+    const int tiles = ((g.M + 255) / 256) * ((g.N + 255) / 256);
+    const int nc = tiles < clusters[dev] ? tiles : clusters[dev];
+    gemm_w8a8_pair_kernel<<<2 * nc, GEMM_THREADS, PAIR_SMEM, stream>>>(ta, tb, g);
+    return check_launch("gemm_w8a8_pair_kernel");
 }
 
 template <int BN>
@@ -278,8 +469,10 @@ int run(const int8_t* A, const int8_t* B, GemmArgs& g, cudaStream_t stream) {
     if (g.N % 8) return fail(B2_ERR_UNSUPPORTED, "gemm: N=%d must be a multiple of 8", g.N);
     if (!aligned16(A) || !aligned16(B)) return fail(B2_ERR_UNSUPPORTED, "gemm: A and B must be 16-byte aligned");
     if (g.M == 0) return B2_OK;
-    // Wide tiles when they fill the machine; half-width tiles when the grid would be too sparse.
+    // CTA pairs on 256 x 256 tiles when they fill the machine; single-CTA tiles for small problems.
     const int tiles256 = ((g.M + BM - 1) / BM) * ((g.N + 255) / 256);
+    if (g.M >= 256 && g.N >= 256 && ((g.M + 255) / 256) * ((g.N + 255) / 256) >= sm_count() / 2)
+        return launch_pair(A, B, g, stream);
     if (tiles256 >= sm_count()) return launch_bn<256>(A, B, g, stream);
     return launch_bn<128>(A, B, g, stream);
 }

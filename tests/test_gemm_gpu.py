@@ -22,8 +22,10 @@ def rand_i8(shape, seed):
     return np.random.default_rng(seed).integers(-128, 128, shape, dtype=np.int8)
 
 
+# The last three have at least 74 tiles of 256 x 256 and run on the CTA-pair kernel (ragged in M and N).
 SHAPES = [(1, 8, 16), (100, 136, 112), (129, 264, 3072), (1000, 256, 256), (300, 520, 160), (128, 256, 128),
-          (257, 1024, 2048), (6642, 256, 3072), (64, 9216, 512)]
+          (257, 1024, 2048), (6642, 256, 3072), (64, 9216, 512), (2048, 2560, 512), (2000, 2600, 384),
+          (6642, 9216, 3072)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -43,7 +45,7 @@ def test_int32_extremes(pkg, dev):
     assert np.array_equal(got, ogemm.int_mm(a, b))
 
 
-@pytest.mark.parametrize("M,N,K", [(77, 264, 384), (1024, 3072, 3072), (513, 128, 8192)])
+@pytest.mark.parametrize("M,N,K", [(77, 264, 384), (1024, 3072, 3072), (513, 128, 8192), (2049, 2568, 512)])
 def test_epilogue_bit_exact(pkg, dev, M, N, K):
     g = np.random.default_rng(M)
     a, b = rand_i8((M, K), 1), rand_i8((N, K), 2)
@@ -57,8 +59,8 @@ def test_epilogue_bit_exact(pkg, dev, M, N, K):
         assert np.array_equal(got.cpu().numpy(), ogemm.epilogue(acc, sa, sw, bb))
 
 
-def test_residual_epilogue_bit_exact(pkg, dev):
-    B, L, N, K = 2, 150, 264, 512
+@pytest.mark.parametrize("B,L,N,K", [(2, 150, 264, 512), (2, 1100, 2816, 256)])
+def test_residual_epilogue_bit_exact(pkg, dev, B, L, N, K):
     M = B * L
     g = np.random.default_rng(5)
     a, b = rand_i8((M, K), 3), rand_i8((N, K), 4)
