@@ -268,17 +268,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             tc_fence_after();
             const int valid = a.Lk - j * TK;
             const float* ks = sKS + (j & 1) * TK;
-            // Pass 1: row max of the scores (log2 domain).
+            // Pass 1: row max of the scores (log2 domain). int8 scores are exact small integers (|dot| < 2^22) and
+            // become fp32 without the conversion pipe. TMEM is read in 32-column pieces so that the destination
+            // registers of tcgen05.ld never need to spill before tcgen05.wait::ld.
+            const bool full = valid >= TK;
             float mx = -1e30f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t v[32];
                 tmem_ld32_wait(tS + c * 32, v);
+                float x[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = c * 32 + i;
-                    const float x = I8 ? __fmul_rn(__fmul_rn((float)(int32_t)v[i], qs_c), ks[col]) : __uint_as_float(v[i]);
-                    if (valid >= TK || col < valid) mx = fmaxf(mx, x);
+                for (int i = 0; i < 32; i += 2) {
+                    if (I8) {
+                        const float2 k2 = *reinterpret_cast<const float2*>(ks + c * 32 + i);
+                        const float2 y = upk2(mul2(mul2(pk2(small_i2f(v[i]), small_i2f(v[i + 1])), pk2(qs_c, qs_c)),
+                                                   pk2(k2.x, k2.y)));
+                        x[i] = y.x;
+                        x[i + 1] = y.y;
+                    } else {
+                        x[i] = __uint_as_float(v[i]);
+                        x[i + 1] = __uint_as_float(v[i + 1]);
+                    }
+                }
+                if (full) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) mx = max3(mx, x[i], x[i + 1]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (c * 32 + i < valid) mx = fmaxf(mx, x[i]);
                 }
             }
             if (!I8) mx *= a.scale_log2;
@@ -304,30 +323,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     }
                 }
             }
-            // Pass 2: p = exp2(s*c - m) (fp16 path) or exp2(s - m) (int8), l sums the fp32 p, P (fp16 pairs) goes
-            // into the columns of S already consumed: chunk c of 32 scores -> columns [16c, 16c + 16).
+            // Pass 2: p = exp2(s*c - m) (fp16 path) or exp2(s - m) (int8), l sums the fp32 p (two running partial
+            // sums), P (fp16 pairs) goes into the columns of S already consumed: 32 scores -> columns [16c, 16c + 16).
+            const uint64_t c2 = I8 ? pk2(1.f, 1.f) : pk2(a.scale_log2, a.scale_log2);
+            const uint64_t nm2 = pk2(-m, -m);
+            uint64_t l2 = pk2(0.f, 0.f);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t v[32], pk[16];
                 tmem_ld32_wait(tS + c * 32, v);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    float p2[2];
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int col = c * 32 + 2 * i + e;
-                        const uint32_t raw = v[2 * i + e];
-                        float p;
-                        if (I8) p = ex2(__fmul_rn(__fmul_rn((float)(int32_t)raw, qs_c), ks[col]) - m);
-                        else p = ex2(fmaf(__uint_as_float(raw), a.scale_log2, -m));
-                        if (valid < TK && col >= valid) p = 0.f;
-                        p2[e] = p;
+                    uint64_t s2;
+                    if (I8) {
+                        const float2 k2 = *reinterpret_cast<const float2*>(ks + c * 32 + 2 * i);
+                        s2 = mul2(mul2(pk2(small_i2f(v[2 * i]), small_i2f(v[2 * i + 1])), pk2(qs_c, qs_c)), pk2(k2.x, k2.y));
+                    } else {
+                        s2 = pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
                     }
-                    l += p2[0] + p2[1];
-                    const __half2 hp = __floats2half2_rn(p2[0], p2[1]);
+                    const float2 e = upk2(fma2(s2, c2, nm2));
+                    float p0 = ex2(e.x), p1 = ex2(e.y);
+                    if (!full) {
+                        if (c * 32 + 2 * i >= valid) p0 = 0.f;
+                        if (c * 32 + 2 * i + 1 >= valid) p1 = 0.f;
+                    }
+                    l2 = add2(l2, pk2(p0, p1));
+                    const __half2 hp = __floats2half2_rn(p0, p1);
                     pk[i] = *reinterpret_cast<const uint32_t*>(&hp);
                 }
                 tmem_st16(tS + c * 16, pk);
+            }
+            {
+                const float2 lf = upk2(l2);
+                l += lf.x + lf.y;
             }
             if (I8) mbar_arrive(&k_empty[j & 1]);  // key scales of this stage are consumed
             tmem_wait_st();

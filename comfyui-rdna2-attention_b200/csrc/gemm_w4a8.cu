@@ -7,13 +7,17 @@
 // Layout: A int8 [M, K] (from the pre-pass), W packed uint8 [N, K/2] (low nibble = even k, two's-complement
 // nibbles in [-8, 7]), group scales fp32 [K/128, N] (the fp16 scales widened once at load time, exact).
 //
-// One CTA per SM, persistent over 128x128 output tiles, 8 warps:
+// One CTA per SM, persistent over 128x128 output tiles, 12 warps (three per SM sub-partition, so up to 168
+// registers each):
 //   warp 0      TMA: A tile (128 x 128 B, 128-byte swizzle), packed W tile (128 x 64 B, 64-byte swizzle) and the
 //               group's 128 scales into a 4-deep ring
-//   warp 1      TMEM owner + tcgen05.mma issuer (kind::i8, M=128, N=128, K=32): one group = one k-block of 128
-//   warps 2..3  converters: unpack the int4 tile to int8 in the 128-byte-swizzled K-major layout the MMA reads
-//   warps 4..7  epilogue: per group, read the int32 partial from TMEM, F = fma(acc, s, F) in registers, re-seed
-//               the TMEM buffer; after the last group, scale by as[m], add bias, store fp16
+//   warp 1      TMEM owner + tcgen05.mma issuer (kind::i8, M=128, N=128, K=32): one group = one k-block of 128,
+//               into one of 4 TMEM partial buffers, so the MMA runs up to three groups ahead of the epilogue
+//   warps 2..3  converters: thread t unpacks rows t and t + 64 of the int4 tile to int8 in the 128-byte-swizzled
+//               K-major layout
+//   warps 4..11 epilogue: two warps per 32-lane TMEM quarter, 64 columns each; per group, read the int32 partial,
+//               F = fma(acc, s, F) in packed fp32 pairs, re-seed the buffer; after the last group, scale by as[m],
+//               add bias, store fp16
 // Each group's partial accumulates on top of 0x4B400000 (the bits of 1.5 * 2^23), so the accumulator read back
 // as fp32 minus 1.5 * 2^23 is acc_g exactly: one FADD instead of an int->float conversion.
 #include "common.cuh"
@@ -32,7 +36,8 @@ constexpr int WP_BYTES = BN * GK / 2;     // 8 KB packed
 constexpr int S_BYTES = BN * 4;           // 512 B scales
 constexpr int OFF_B = A_BYTES, OFF_WP = A_BYTES + B_BYTES, OFF_S = OFF_WP + WP_BYTES;
 constexpr int STAGE_BYTES = 41 * 1024;    // 16 + 16 + 8 KB + 512 B, 1024-aligned stride
-constexpr int W4_THREADS = 256;
+constexpr int W4_THREADS = 384;
+constexpr int NPB = 4;  // TMEM partial buffers of 128 columns
 constexpr int SMEM = STAGES * STAGE_BYTES + 256 + 1024;
 constexpr uint32_t SEED = 0x4B400000u;
 constexpr float SEED_F = 12582912.0f;
@@ -64,9 +69,9 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
     uint64_t* full = bars;                 // [STAGES] TMA landed
     uint64_t* conv = bars + STAGES;        // [STAGES] int8 B tile written
     uint64_t* empty = bars + 2 * STAGES;   // [STAGES] MMA done + epilogue read the scales
-    uint64_t* pready = bars + 3 * STAGES;  // [2] partial complete in TMEM
-    uint64_t* pfree = pready + 2;          // [2] partial consumed and re-seeded
-    uint64_t* drain = pfree + 2;
+    uint64_t* pready = bars + 3 * STAGES;  // [NPB] partial complete in TMEM
+    uint64_t* pfree = pready + NPB;        // [NPB] partial consumed and re-seeded
+    uint64_t* drain = pfree + NPB;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -79,11 +84,11 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&conv[s], 64);
-            mbar_init(&empty[s], 1 + 128);
+            mbar_init(&empty[s], 1 + 8);  // the MMA commit and one arrival per epilogue warp (scales read)
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NPB; ++b) {
             mbar_init(&pready[b], 1);
-            mbar_init(&pfree[b], 128);
+            mbar_init(&pfree[b], 8);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
         tma_prefetch_desc(&tmS);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 256);
+        tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -142,8 +147,8 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
                 for (int kb = 0; kb < G; ++kb, ++q) {
-                    const uint32_t b = q & 1;
-                    if (!mbar_wait(&pfree[b], (q >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA) ||
+                    const uint32_t b = q % NPB;
+                    if (!mbar_wait(&pfree[b], (q / NPB) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA) ||
                         !mbar_wait(&full[stage], phase, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA) ||
                         !mbar_wait(&conv[stage], phase, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) {
                         ok = false;
@@ -180,8 +185,8 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
                 }
                 unsigned char* st = smem + stage * STAGE_BYTES;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = t + 64 * h;
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int r = t + 64 * hr;
                     const unsigned char* src = st + OFF_WP + r * 64;
                     unsigned char* dst = st + OFF_B + r * 128;
 #pragma unroll
@@ -201,50 +206,59 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
             if (!ok) break;
         }
     } else {
-        // Epilogue: thread -> row (quarter * 32 + lane), 128 fp32 accumulators in registers.
+        // Epilogue: warp -> (32-lane quarter, 64-column half); thread -> row, 64 fp32 accumulators in 32 pairs.
         const int quarter = warp & 3;
+        const int half = (warp - 4) >> 2;
         const int r = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        uint32_t seed[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) seed[i] = SEED;
+        for (int b = 0; b < NPB; ++b)
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c) tmem_st32(tmem + lane_base + b * BN + c * 32, seed);
+            for (int c = 0; c < 2; ++c) tmem_fill32(tmem + lane_base + b * BN + half * 64 + c * 32, SEED);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&pfree[0]);
-        mbar_arrive(&pfree[1]);
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < NPB; ++b) mbar_arrive(&pfree[b]);
+        const uint64_t nseed = pk2(-SEED_F, -SEED_F);
         int stage = 0;
         uint32_t q = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
-            float F[BN];
+            const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN + half * 64;
+            uint64_t F[32];
 #pragma unroll
-            for (int i = 0; i < BN; ++i) F[i] = 0.f;
+            for (int i = 0; i < 32; ++i) F[i] = 0ull;
             for (int kb = 0; kb < G; ++kb, ++q) {
-                const uint32_t b = q & 1;
-                if (!mbar_wait(&pready[b], (q >> 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                const uint32_t b = q % NPB;
+                if (!mbar_wait(&pready[b], (q / NPB) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const float* sc = reinterpret_cast<const float*>(smem + stage * STAGE_BYTES + OFF_S);
+                const float4* sc = reinterpret_cast<const float4*>(smem + stage * STAGE_BYTES + OFF_S) + half * 16;
 #pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32_wait(tmem + lane_base + b * BN + c * 32, v);
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t v[16];
+                    tmem_ld16_wait(tmem + lane_base + b * BN + half * 64 + c * 16, v);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        F[c * 32 + i] = fmaf(__uint_as_float(v[i]) - SEED_F, sc[c * 32 + i], F[c * 32 + i]);
-                    tmem_st32(tmem + lane_base + b * BN + c * 32, seed);
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 s4 = sc[c * 4 + i];
+                        const uint64_t a0 = add2(pk2(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), nseed);
+                        const uint64_t a1 = add2(pk2(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), nseed);
+                        F[c * 8 + 2 * i] = fma2(a0, pk2(s4.x, s4.y), F[c * 8 + 2 * i]);
+                        F[c * 8 + 2 * i + 1] = fma2(a1, pk2(s4.z, s4.w), F[c * 8 + 2 * i + 1]);
+                    }
                 }
+#pragma unroll
+                for (int c = 0; c < 2; ++c) tmem_fill32(tmem + lane_base + b * BN + half * 64 + c * 32, SEED);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&pfree[b]);
-                mbar_arrive(&empty[stage]);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&pfree[b]);
+                    mbar_arrive(&empty[stage]);
+                }
                 if (++stage == STAGES) stage = 0;
             }
             if (!ok) break;
@@ -253,11 +267,15 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
                 const float sa = g.as[m];
                 __half* dst = g.C + (int64_t)m * g.N + n0;
 #pragma unroll
-                for (int j = 0; j < BN / 8; ++j) {
-                    if (n0 + 8 * j >= g.N) break;
+                for (int j = 0; j < 8; ++j) {
+                    if (n0 + 8 * j >= g.N) continue;  // (not break: F must stay register-indexed)
                     float y[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) y[e] = __fmul_rn(F[8 * j + e], sa);
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = upk2(F[4 * j + e]);
+                        y[2 * e] = __fmul_rn(f.x, sa);
+                        y[2 * e + 1] = __fmul_rn(f.y, sa);
+                    }
                     if (g.bias) {
                         const uint4 braw = __ldg(reinterpret_cast<const uint4*>(g.bias + n0 + 8 * j));
                         const __half2* bh = reinterpret_cast<const __half2*>(&braw);
@@ -281,7 +299,7 @@ __global__ void __launch_bounds__(W4_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 256);
+    if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 }  // namespace

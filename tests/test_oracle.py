@@ -172,3 +172,4 @@ def test_quant_rows_rint_is_half_even():
     x[0, 3] = -2.5
     q, s = oatt.quant_rows_rint(x)
     assert s[0] == 1.0 and q[0, :4].tolist() == [127, 0, 2, -2]
+
