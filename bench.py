@@ -30,6 +30,18 @@ if ROOT not in sys.path:
 
 L2_BYTES = 126 * 1024 * 1024
 
+# DRAM traffic per launch of each workload's roofline kernel: dram__bytes_read.sum + dram__bytes_write.sum from one
+# ncu capture of that kernel on a B200 (cold L2).  Output lines still dirty in L2 when a kernel ends are not counted
+# as written yet, so a kernel whose output fits in L2 can show less than its algorithmic bytes.
+NCU_TRAFFIC = {
+    "attn": 149.61e6 + 29.04e6,      # C2 fp16, one launch
+    "attn_i8": 101.35e6 + 23.09e6,   # C2 int8 QK, one launch
+    "w4a8": 22.17e6 + 0.60e6,        # C3, one launch
+    "prepass": 40.86e6 + 0.25e6,     # C4 QKV pre-pass (MOD), one launch; the 20.4 MB int8 output stays in L2
+    "decode": 15.78e6 * 19456 / 6144,  # captured on the 6144-row qkv GEMV; bytes grow with rows (2568 B per row)
+    "dit": 112.50e6 + 69.24e6,       # mean over the 32 W8A8 GEMM launches of one DiT step
+}
+
 
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -301,7 +313,7 @@ class AttnC2:
         peak = peaks["bf16_tflops"]
         achieved = self.flops / (kms * 1e-3) / 1e12
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "traffic": None, "kernel": "attention_kernel",
+                "traffic": NCU_TRAFFIC["attn_i8" if self.int8_qk else "attn"], "kernel": "attention_kernel",
                 "note": f"fp16 peak = {peaks['source']} bf16 dense" + ("; includes the int8 Q/K quantization" if self.int8_qk else "")}
 
     @staticmethod
@@ -381,7 +393,7 @@ class W4A8C3:
         peak = 2.0 * peaks["bf16_tflops"]
         achieved = self.ops_per_step / (kms * 1e-3) / 1e12
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS", "frac": achieved / peak,
-                "traffic": None, "kernel": "gemm_w4a8_kernel",
+                "traffic": NCU_TRAFFIC["w4a8"], "kernel": "gemm_w4a8_kernel",
                 "note": f"int8 peak = 2 x {peaks['source']} bf16 ({peaks['bf16_tflops']} TFLOP/s)"}
 
     @staticmethod
@@ -467,7 +479,7 @@ class PrepassC4:
     def roofline(self, peaks, kms):
         achieved = self.bytes / (kms * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "prepass_kernel<MOD,128>",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["prepass"], "kernel": "prepass_kernel<MOD,128>",
                 "note": f"{peaks['source']} HBM copy bandwidth"}
 
     @staticmethod
@@ -540,7 +552,8 @@ class DecodeC5:
     def roofline(self, peaks, kms):
         achieved = self.gemv_bytes / (kms * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "gemv_i8_kernel (gate|up, 19456 x 2560)",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["decode"],
+                "kernel": "gemv_i8_kernel (gate|up, 19456 x 2560)",
                 "note": f"{peaks['source']} HBM copy bandwidth; step bytes {self.bytes / 1e9:.3f} GB per token"}
 
     @staticmethod
@@ -684,7 +697,7 @@ class DiTC4:
             comp[kind] = c
         step_roof_ms = (self.lin_ops / (int8_peak * 1e12) + self.att_flops / (peaks["bf16_tflops"] * 1e12)) * 1e3
         return {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
-                "traffic": None, "kernel": "gemm_w8a8_kernel (all 32 GEMM launches of a step)",
+                "traffic": NCU_TRAFFIC["dit"], "kernel": "gemm_w8a8_kernel (all 32 GEMM launches of a step)",
                 "note": f"int8 peak = 2 x {peaks['source']} bf16 ({peaks['bf16_tflops']} TFLOP/s)",
                 "components": comp, "step_roofline_ms": step_roof_ms}
 
