@@ -165,6 +165,316 @@ __device__ __forceinline__ int quant1(float f, float scale, float inv) {
     return __float_as_int(__fadd_rn(r, 12582912.f)) - 0x4B400000;
 }
 
+// ------------------------------------------------------------------------------------------- block-128, K % 1024
+// Rows whose K is a multiple of 1024 under the block-128 rotation: a CTA of K/32 threads holds one row in
+// registers (many CTAs per SM hide the load latency; a grid-stride walk with a prefetch of the next row needed so
+// many registers that fewer rows were in flight). Thread t owns a
+// quarter of 128-block t/4: with s = t%4 it loads the four 16-byte runs at 128 (t/4) + 32 o + 8 s (o = 0..3), so
+// block index bits 0-2 (e) and 5-6 (o) are in registers and bits 3-4 (s) span the block's 4 threads. Bits 0-2 are
+// rotated first; a per-warp 4 KB shared-memory transpose then trades bits 1-2 for the thread bits, and bits 3-6
+// finish in registers. Butterflies run on packed fp32 pairs (bit 5 on the two halves of a pair) in the Sylvester
+// order, bit 0 first, so every fp32 result equals the one-bit-at-a-time reference exactly. The fp16 row waits in
+// registers for the CTA's absmax (one barrier), is quantized in place (quant_fast) and leaves through a 1 KB
+// per-warp byte transpose as 16-byte stores. Both transposes are free of shared-memory bank conflicts.
+constexpr int R128_WARP_BYTES = 4096 + 1024;
+constexpr int R128_MAX_WARPS = MAX_K / 1024;
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint64_t h2_to_f2(uint32_t h) {
+    const float2 f = __half22float2(u32_as_h2(h));
+    return pk2(f.x, f.y);
+}
+__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
+    const float2 f = upk2(v);
+    return h2_as_u32(__floats2half2_rn(f.x, f.y));
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// max(a, |b|, |c|) with NaN propagation: any NaN operand gives NaN.
+__device__ __forceinline__ float max3_abs_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(fabsf(b)), "f"(fabsf(c)));
+    return d;
+}
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+
+// 1 / (1 + exp(-g)) for a pair: exp(-g) = 2^(-g log2 e) with the hardware base-2 approximation, then the hardware
+// reciprocal approximation (a few fp32 ulps, like the per-value silu_mul / sigmoid_gate above).
+__device__ __forceinline__ uint64_t sigmoid2(uint64_t G) {
+    const float2 m = upk2(mul2(G, splat2(-1.4426950408889634f)));
+    const float2 d = upk2(add2(pk2(ex2_approx(m.x), ex2_approx(m.y)), splat2(1.f)));
+    return pk2(rcp_approx(d.x), rcp_approx(d.y));
+}
+
+__device__ __forceinline__ void bfly2(uint64_t& a, uint64_t& b) {
+    const uint64_t x = a, y = b;
+    a = add2(x, y);
+    b = sub2(x, y);
+}
+// The butterfly between the two halves of one pair.
+__device__ __forceinline__ void bfly_in(uint64_t& a) {
+    const float2 f = upk2(a);
+    a = pk2(__fadd_rn(f.x, f.y), __fsub_rn(f.x, f.y));
+}
+
+// Quantization with one fma per value: t = fma(y, 1/scale, 1.5 * 2^23) rounds y/scale to the nearest integer q (ties
+// to even) and holds q in its low mantissa bits, so the int8 byte is t's low byte. That equals the reference's
+// floor(y / scale + 0.5) unless y/scale lies within 1e-4 of a half-integer (|y/scale| <= 127 keeps the product within
+// 8e-6 of the IEEE quotient): d = y/scale - q tells, and the caller sends a thread whose largest |d| exceeds 0.4999
+// (or is NaN, from a non-finite y) through quant1. F is the fp32 pair of one fp16 pair; returns T, accumulates |d|.
+__device__ __forceinline__ uint64_t quant_fast(uint64_t F, uint64_t inv2, float& dmax) {
+    const uint64_t C = splat2(12582912.f);
+    const uint64_t T = fma2(F, inv2, C);
+    const float2 d = upk2(fma2(F, inv2, fma2(T, splat2(-1.f), C)));
+    dmax = max3_abs_nan(dmax, d.x, d.y);
+    return T;
+}
+
+template <int ACT>
+__global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ float red[2][R128_MAX_WARPS];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int K = a.K;
+    const int s = lane & 3, bw = lane >> 2;  // quarter within the block, block within the warp
+    const int k0 = (tid >> 2) * 128 + s * 8;
+    float* T = reinterpret_cast<float*>(smem + warp * R128_WARP_BYTES);
+    unsigned char* B8 = smem + warp * R128_WARP_BYTES + 4096;
+    constexpr bool TWO = ACT == ACT_SWIGLU || ACT == ACT_GATE;
+
+    uint4 rx[4], ru[4];
+    auto load_row = [&](int r) {
+        const __half* xr = a.x + (int64_t)r * a.ldx;
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+            const int k = k0 + 32 * o;
+            rx[o] = ldg_stream(a.seg ? xr + (int64_t)(k / a.seg) * a.seg_stride + (k % a.seg) : xr + k);
+            if (TWO) ru[o] = ldg_stream(a.u + (int64_t)r * a.ldu + k);
+        }
+    };
+
+    const int row = blockIdx.x;
+    load_row(row);
+    {
+        // y[o][p]: the activation's fp16 pair at k0 + 32 o + 2 p.
+        uint32_t y[4][4];
+        if (ACT == ACT_MOD) {
+            uint64_t X[4][4];
+            uint64_t ss2 = splat2(0.f);
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(&rx[o]);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    X[o][p] = h2_to_f2(w[p]);
+                    ss2 = fma2(X[o][p], X[o][p], ss2);
+                }
+            }
+            const float2 sp = upk2(ss2);
+            float ss = sp.x + sp.y;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            if (lane == 0) red[0][warp] = ss;
+            __syncthreads();
+            ss = 0.f;
+            for (int w = 0; w < nwarps; ++w) ss += red[0][w];
+            const uint64_t R2 = splat2(rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
+            const __half* srow = a.s + (int64_t)(row / a.L) * K;
+            const __half* trow = a.t + (int64_t)(row / a.L) * K;
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                const int k = k0 + 32 * o;
+                const uint4 sv = __ldg(reinterpret_cast<const uint4*>(srow + k));
+                const uint4 tv = __ldg(reinterpret_cast<const uint4*>(trow + k));
+                const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.w + k));
+                const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.w + k) + 1);
+                const uint64_t W[4] = {pk2(w0.x, w0.y), pk2(w0.z, w0.w), pk2(w1.x, w1.y), pk2(w1.z, w1.w)};
+                const uint32_t* s2 = reinterpret_cast<const uint32_t*>(&sv);
+                const uint32_t* t2 = reinterpret_cast<const uint32_t*>(&tv);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    // n = fp16(x rstd (w + 1)); y = fp16(fp16(n s) + t) as exact fp16 pair operations (see
+                    // prepass_kernel)
+                    const uint32_t n = f2_to_h2(mul2(mul2(X[o][p], R2), add2(W[p], splat2(1.f))));
+                    y[o][p] = h2_as_u32(__hadd2_rn(__hmul2_rn(u32_as_h2(n), u32_as_h2(s2[p])), u32_as_h2(t2[p])));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                const uint32_t* xw = reinterpret_cast<const uint32_t*>(&rx[o]);
+                const uint32_t* uw = reinterpret_cast<const uint32_t*>(&ru[o]);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    if (ACT == ACT_SWIGLU) {
+                        // fp16(fp16(g sigmoid(g)) u): a product of two fp16 values rounded once is the fp32 path's
+                        const uint64_t G = h2_to_f2(xw[p]);
+                        const uint32_t silu = f2_to_h2(mul2(G, sigmoid2(G)));
+                        y[o][p] = h2_as_u32(__hmul2_rn(u32_as_h2(silu), u32_as_h2(uw[p])));
+                    } else if (ACT == ACT_GATE) {
+                        const uint32_t sig = f2_to_h2(sigmoid2(h2_to_f2(uw[p])));
+                        y[o][p] = h2_as_u32(__hmul2_rn(u32_as_h2(xw[p]), u32_as_h2(sig)));
+                    } else {
+                        y[o][p] = xw[p];
+                    }
+                }
+            }
+        }
+        if (ACT != ACT_NONE && a.act_out) {
+#pragma unroll
+            for (int o = 0; o < 4; ++o)
+                *reinterpret_cast<uint4*>(a.act_out + (int64_t)row * K + k0 + 32 * o) =
+                    make_uint4(y[o][0], y[o][1], y[o][2], y[o][3]);
+        }
+
+        // Bits 0-2 on pairs P[h][e] = (value of o = 2h, value of o = 2h + 1) at e.
+        uint64_t P[2][8];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const float2 lo = __half22float2(u32_as_h2(y[2 * h][p]));
+                const float2 hi = __half22float2(u32_as_h2(y[2 * h + 1][p]));
+                P[h][2 * p] = pk2(lo.x, hi.x);
+                P[h][2 * p + 1] = pk2(lo.y, hi.y);
+            }
+#pragma unroll
+        for (int st = 1; st < 8; st <<= 1)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    if (!(e & st)) bfly2(P[h][e], P[h][e + st]);
+
+        // Transpose: row R = 4 bw + e/2 of the warp's buffer receives the 4 values (o = 0..3) of (s, e) as its
+        // logical 16-byte chunk 2 s + e%2; chunks are XOR-swizzled with g(R) = (R & 7) ^ ((R >> 2) & 1).
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int R = 4 * bw + (e >> 1);
+            const int chunk = (2 * s + (e & 1)) ^ ((R & 7) ^ ((R >> 2) & 1));
+            const float2 lo = upk2(P[0][e]), hi = upk2(P[1][e]);
+            *reinterpret_cast<float4*>(T + R * 32 + chunk * 4) = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+        __syncwarp();
+        // Q[j][i][h] = the pair (o = 2h, o = 2h + 1) of element 32 o + 8 j + 2 s + i of this thread's block:
+        // bits 3-4 are j, bit 0 is i, bit 5 is inside the pair and bit 6 is h.
+        uint64_t Q[4][2][2];
+        {
+            const int gl = (lane & 7) ^ ((lane >> 2) & 1);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 f = *reinterpret_cast<const float4*>(T + lane * 32 + ((c ^ gl) << 2));
+                Q[c >> 1][c & 1][0] = pk2(f.x, f.y);
+                Q[c >> 1][c & 1][1] = pk2(f.z, f.w);
+            }
+        }
+#pragma unroll
+        for (int st = 1; st < 4; st <<= 1)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        if (!(j & st)) bfly2(Q[j][i][h], Q[j + st][i][h]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                bfly_in(Q[j][i][0]);
+                bfly_in(Q[j][i][1]);
+                bfly2(Q[j][i][0], Q[j][i][1]);
+            }
+
+        // y = fp16(v / sqrt(128)); max |y| = fp16(max |v / sqrt(128)|) since rounding is monotonic (a NaN is skipped,
+        // as the reference's fmaxf chain skips it).
+        uint32_t yq[4][2][2];
+        float mxf = 0.f;
+        const uint64_t C2 = splat2(INV_SQRT128);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t V = mul2(Q[j][i][h], C2);
+                    const float2 v = upk2(V);
+                    mxf = max3(mxf, fabsf(v.x), fabsf(v.y));
+                    yq[j][i][h] = f2_to_h2(V);
+                }
+        float mx = round_h(mxf);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        float* redm = red[1];
+        if (lane == 0) redm[warp] = mx;
+        __syncthreads();
+        mx = 0.f;
+        for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, redm[w]);
+        const float scale = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
+        const float inv = __frcp_rn(scale);
+        if (tid == 0) a.scale[row] = scale;
+
+        // qb[o][j]: bytes of elements 32 o + 8 j + 2 s + {0, 1}.
+        uint32_t qb[4][4];
+        float dmax = 0.f;
+        const uint64_t inv2 = splat2(inv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float2 t0 = upk2(quant_fast(h2_to_f2(yq[j][0][h]), inv2, dmax));
+                const float2 t1 = upk2(quant_fast(h2_to_f2(yq[j][1][h]), inv2, dmax));
+                qb[2 * h][j] = __byte_perm(__float_as_uint(t0.x), __float_as_uint(t1.x), 0x0040);
+                qb[2 * h + 1][j] = __byte_perm(__float_as_uint(t0.y), __float_as_uint(t1.y), 0x0040);
+            }
+        if (!(dmax <= 0.4999f)) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float2 f0 = __half22float2(u32_as_h2(yq[j][0][h]));
+                    const float2 f1 = __half22float2(u32_as_h2(yq[j][1][h]));
+                    qb[2 * h][j] = (uint32_t)(quant1(f0.x, scale, inv) & 255) | ((uint32_t)(quant1(f1.x, scale, inv) & 255) << 8);
+                    qb[2 * h + 1][j] =
+                        (uint32_t)(quant1(f0.y, scale, inv) & 255) | ((uint32_t)(quant1(f1.y, scale, inv) & 255) << 8);
+                }
+        }
+
+        // Byte transpose: logical byte 32 o + 8 j + 2 s of block bw, 16-byte chunks XOR-swizzled with f(bw).
+        const int fb = ((bw & 1) << 2) | (bw >> 1);
+#pragma unroll
+        for (int o = 0; o < 4; ++o)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int L = 32 * o + 8 * j + 2 * s;
+                *reinterpret_cast<uint16_t*>(B8 + bw * 128 + (((L >> 4) ^ fb) << 4) + (L & 15)) = (uint16_t)qb[o][j];
+            }
+        __syncwarp();
+        int8_t* qrow = a.q + (int64_t)row * K + warp * 1024 + bw * 128;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            *reinterpret_cast<uint4*>(qrow + h * 64 + s * 16) =
+                *reinterpret_cast<const uint4*>(B8 + bw * 128 + (((4 * h + s) ^ fb) << 4));
+    }
+}
+
 template <int ACT, int ROT>
 __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const PrepassArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -399,8 +709,24 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
     }
 }
 
+template <int ACT>
+int launch_r128(const PrepassArgs& a, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        int rc = set_smem(prepass128_kernel<ACT>, R128_MAX_WARPS * R128_WARP_BYTES);
+        if (rc) return rc;
+        configured[dev] = true;
+    }
+    const int warps = a.K / 1024;
+    prepass128_kernel<ACT><<<a.M, warps * 32, warps * R128_WARP_BYTES, stream>>>(a);
+    return check_launch("prepass128_kernel");
+}
+
 template <int ACT, int ROT>
 int launch_t(const PrepassArgs& a, cudaStream_t stream) {
+    if (ROT == 128 && a.K % 1024 == 0) return launch_r128<ACT>(a, stream);
     const int smem = PP_WARPS * (a.K * 2 + T_BYTES);
     static bool configured[64] = {false};
     int dev = 0;

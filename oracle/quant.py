@@ -19,7 +19,8 @@ def quant_rows(y):
     float32 [M]).
     """
     f = np.asarray(y).astype(F32)
-    mx = np.abs(f).max(axis=1) if f.shape[1] else np.zeros(f.shape[0], F32)
+    # The absmax is a chain of fmaxf starting at 0 (:96-100, :32-37): a NaN value never wins it.
+    mx = np.fmax.reduce(np.abs(f), axis=1, initial=F32(0)) if f.shape[1] else np.zeros(f.shape[0], F32)
     scale = np.maximum(mx / F32(127), F32(1e-30)).astype(F32)
     with np.errstate(invalid="ignore", divide="ignore"):
         q = np.floor(f / scale[:, None] + F32(0.5))

@@ -22,6 +22,14 @@ def test_quant_rounds_half_up_after_ieee_divide():
     assert q.tolist() == [[127, 1, 0, 2, -1, 3, -2, -127]]
 
 
+def test_quant_nan_never_wins_absmax():
+    # int8_gemm.hip:96-100,32-37: mx = fmaxf chain from 0, so a NaN is skipped; fmaxf(NaN, -128) = -128 (:53).
+    row = np.array([[np.nan, 2.54, -1.27, 0]], dtype=F16)
+    q, s = oq.quant_rows(row)
+    assert s[0] == np.float32(np.float16(2.54)) / np.float32(127)
+    assert q.tolist() == [[-128, 127, -63, 0]]
+
+
 def test_quant_zero_row_uses_scale_floor():
     q, s = oq.quant_rows(np.zeros((2, 16), F16))
     assert np.all(s == F32(1e-30)) and not q.any()

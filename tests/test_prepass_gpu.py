@@ -40,14 +40,18 @@ def test_quant_bit_exact(pkg, dev, rot, M, K):
     assert np.array_equal(q.cpu().numpy(), q_ref)
 
 
-def test_quant_edge_values(pkg, dev):
-    K = 256
-    x = np.zeros((6, K), F16)
-    x[1, :] = 65504                      # fp16 max
+@pytest.mark.parametrize("K", [256, 1024])
+def test_quant_edge_values(pkg, dev, K):
+    x = np.zeros((8, K), F16)
+    x[1, :] = 65504                      # fp16 max: the rotation overflows fp16 to inf
     x[2, ::2] = 6e-8                     # subnormal fp16
     x[3, :8] = [127, 0.5, -0.5, 1.5, -1.5, 2.5, -2.5, -127]  # half-up ties with scale 1
     x[4] = np.linspace(-3, 3, K).astype(F16)
     x[5, 17] = -1
+    x[6] = np.linspace(-1, 1, K).astype(F16)
+    x[6, 130] = np.nan                   # NaN never wins the absmax and quantizes to -128
+    x[7] = np.linspace(-2, 2, K).astype(F16)
+    x[7, 5] = -np.inf
     for rot in (0, 128, 256):
         q, s = pkg.ops.quant_pack_a(dev_(x, dev), rot)
         q_ref, s_ref, _ = oq.prepass(x, rot)
@@ -104,7 +108,7 @@ def test_swiglu_prepass(pkg, dev, rot):
     _check_act(pkg, dev, act, oq.swiglu(gate, up), q, s, rot)
 
 
-@pytest.mark.parametrize("rot", [0, 256])
+@pytest.mark.parametrize("rot", [0, 128, 256])
 def test_gate_prepass(pkg, dev, rot):
     M, K = 65, 3072
     g = np.random.default_rng(12)
