@@ -807,13 +807,14 @@ def main():
     kms = kernel_ms(wl.events) if not isinstance(wl, DiTC4) else None
 
     with Clocks(local) as clocks:
-        # Pre-roll under the sampler so that the clock record covers the load of the timed region that follows.
+        # Pre-roll under the sampler so that the clock record covers the load of the timed region that follows. The
+        # step count is agreed over ranks (the largest), so every rank issues the same collectives.
         clocks.wait_first()
-        t_end, i = time.time() + 1.0, 0
-        while time.time() < t_end:
+        pre = max(1, math.ceil(1000.0 / max(timed(wl.step, 1, 0, world), 1e-3)))
+        pre = int(max_over_ranks(float(pre), world))
+        for i in range(pre):
             wl.step(i)
-            torch.cuda.synchronize()
-            i += 1
+        torch.cuda.synchronize()
         ms = timed(wl.step, args.steps, args.warmup, world)
     e2e_ms = timed(wl.e2e_step, args.steps, args.warmup, world)
 
@@ -827,7 +828,7 @@ def main():
                     "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
             "roofline": wl.roofline(peaks, kms), "kernel_ms": kms, "clocks": clocks.summary(),
             "gpu_launches": wl.launches_per_step * args.steps}
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample = type(wl).cpu_baseline(os.cpu_count() or 1) if hasattr(type(wl), "cpu_baseline") else (None, "")
         line["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": os.cpu_count(), "kind": "port", "sample": sample}
     if rank == 0:
