@@ -129,6 +129,24 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
+// Tiled store of a shared-memory box (bulk-group completion). The box start must be >= 0 in every coordinate.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's committed bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of this thread's committed bulk groups are incomplete (writes included).
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 // L2 policy: keep weights (re-read by every row tile) and let streamed activations go first.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t p;
@@ -378,6 +396,17 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
     return d;
 }
 __device__ __forceinline__ uint64_t splat2(float a) { return pk2(a, a); }
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+// fp16 pair <-> fp32 pair (exact one way, round-to-nearest-even the other).
+__device__ __forceinline__ uint64_t h2_to_f2(uint32_t h) {
+    const float2 f = __half22float2(u32_as_h2(h));
+    return pk2(f.x, f.y);
+}
+__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
+    const float2 f = upk2(v);
+    return h2_as_u32(__floats2half2_rn(f.x, f.y));
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

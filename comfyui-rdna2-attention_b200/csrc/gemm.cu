@@ -9,7 +9,7 @@
 //   warp 0      TMA producer: 128x128 A tiles and BNx128 B tiles (128-byte swizzle) into a STAGES-deep ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=BN, K=32 per instruction)
 //   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (each warp its 32-lane quarter), dequant,
-//               bias, residual, fp16 stores
+//               bias, residual, fp16 through a swizzled shared-memory box and one TMA store per 32 x 32 box
 // Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the main loop of tile i+1.
 #include "common.cuh"
 #include "host.hpp"
@@ -23,6 +23,12 @@ constexpr int BM = 128;
 constexpr int BK = 128;  // bytes = int8 values per k-block (one 128-byte swizzle atom)
 constexpr int GEMM_THREADS = 192;
 
+// Epilogue staging: per epilogue warp EPI_BUFS boxes of 32 rows x 64 bytes (32 fp16 columns).
+constexpr int EPI_BUFS = 3;
+constexpr int EPI_BUF_BYTES = 32 * 64;
+constexpr int EPI_WARP_BYTES = EPI_BUFS * EPI_BUF_BYTES;
+constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
+
 template <int BN>
 struct Cfg {
     static constexpr int STAGES = BN == 256 ? 4 : 6;
@@ -30,8 +36,8 @@ struct Cfg {
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int BAR_BYTES = 512;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;
 };
 
 struct GemmArgs {
@@ -46,78 +52,167 @@ struct GemmArgs {
     int M, N, K;
 };
 
-// 32 accumulator columns of one row: dequant (+ bias) (+ residual) -> fp16, or raw int32.
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, uint32_t taddr, int m, bool row_ok, float sa, int nb) {
+// 32 raw int32 accumulator columns of one row (the debugging output C32), stored from registers.
+__device__ __forceinline__ void epilogue_chunk_i32(const GemmArgs& g, uint32_t taddr, int m, bool row_ok, int nb) {
     uint32_t r[32];
     tmem_ld32_wait(taddr, r);
     if (!row_ok || nb >= g.N) return;
-    if (g.C32) {
-        int32_t* dst = g.C32 + (int64_t)m * g.N + nb;
+    int32_t* dst = g.C32 + (int64_t)m * g.N + nb;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (nb + 4 * j < g.N)
-                *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-        return;
-    }
-    __half* dst = g.C + (int64_t)m * g.N + nb;
-    const __half* res = g.R ? g.R + (int64_t)m * g.N + nb : nullptr;
-    const __half* gate = g.R ? g.G + (int64_t)(m / g.L) * g.N + nb : nullptr;
+    for (int j = 0; j < 8; ++j)
+        if (nb + 4 * j < g.N)
+            *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+}
+
+// One epilogue warp's share of a tile: 32 accumulator rows (TMEM lanes of the warp's quarter) x ncols columns,
+// 32 columns at a time. Row `lane` of the chunk is dequantized in registers and written into a staging box with the
+// 64-byte swizzle (16-byte piece j of row r at piece j ^ ((r >> 1) & 3): the row-per-lane writes are free of bank
+// conflicts), and lane 0 stores the 32 x 32 box with one TMA store, so the output leaves in whole lines (TMA clips
+// rows >= M and columns >= N). With a residual, lane 0 brings the matching box of R in by TMA one chunk ahead into
+// the next box. The warp's n-th chunk uses box n % 3; a box is refilled only after the store that last read it is
+// done reading (bulk_wait_read), and every R load is waited for before the function returns.
+struct EpiCtx {
+    unsigned char* buf;  // EPI_BUFS boxes
+    uint64_t* rbar;      // EPI_BUFS barriers for the residual loads
+    uint32_t n;          // chunks this warp has processed
+    uint32_t inflight;   // bit b: a residual load into box b is in flight; bit 8 + b: its phase parity
+};
+
+__device__ __forceinline__ void epi_load_r(const CUtensorMap* tmR, EpiCtx& e, uint32_t chunk, int col, int row0) {
+    const uint32_t b = chunk % EPI_BUFS;
+    mbar_arrive_expect_tx(&e.rbar[b], EPI_BUF_BYTES);
+    tma_load_2d(e.buf + b * EPI_BUF_BYTES, tmR, &e.rbar[b], col, row0);
+    e.inflight = (e.inflight & ~(0x101u << b)) | (1u << b) | ((((chunk / EPI_BUFS) & 1u)) << (8 + b));
+}
+
+__device__ __noinline__ void epi_drain(EpiCtx& e) {
+    for (int b = 0; b < EPI_BUFS; ++b)
+        if (e.inflight & (1u << b))
+            if (!mbar_wait_drain(&e.rbar[b], (e.inflight >> (8 + b)) & 1, 100000000ull))
+                atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
+    e.inflight = 0;
+}
+
+// Per-column scale, bias and (per row) gate of 32 columns. Columns past N are clamped to the last group of 8 (N % 8
+// == 0); their results are never stored.
+struct EpiParams {
+    float4 w[8];
+    uint4 b[4];
+    uint4 gt[4];
+};
+
+__device__ __forceinline__ void epi_params(const GemmArgs& g, const __half* gate_row, int nb, EpiParams& p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        if (nb + 8 * j >= g.N) break;
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j));
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(g.ws + nb + 8 * j) + 1);
-        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (g.bias) {
-            const uint4 braw = __ldg(reinterpret_cast<const uint4*>(g.bias + nb + 8 * j));
-            const __half2* bh = reinterpret_cast<const __half2*>(&braw);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __half22float2(bh[e]);
-                bv[2 * e] = f.x;
-                bv[2 * e + 1] = f.y;
-            }
-        }
-        float y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const float v = __fmul_rn(__fmul_rn((float)(int32_t)r[8 * j + e], sa), wv[e]);
-            y[e] = round_h(g.bias ? __fadd_rn(v, bv[e]) : v);
-        }
-        if (res) {
-            const uint4 rraw = *reinterpret_cast<const uint4*>(res + 8 * j);
-            const uint4 graw = __ldg(reinterpret_cast<const uint4*>(gate + 8 * j));
-            const __half2* rh = reinterpret_cast<const __half2*>(&rraw);
-            const __half2* gh = reinterpret_cast<const __half2*>(&graw);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 rf = __half22float2(rh[e]), gf = __half22float2(gh[e]);
-                y[2 * e] = round_h(__fadd_rn(rf.x, round_h(__fmul_rn(gf.x, y[2 * e]))));
-                y[2 * e + 1] = round_h(__fadd_rn(rf.y, round_h(__fmul_rn(gf.y, y[2 * e + 1]))));
-            }
-        }
-        uint4 o;
-        __half2* oh = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
-        *reinterpret_cast<uint4*>(dst + 8 * j) = o;
+        const int col = min(nb + 8 * j, g.N - 8);
+        p.w[2 * j] = __ldg(reinterpret_cast<const float4*>(g.ws + col));
+        p.w[2 * j + 1] = __ldg(reinterpret_cast<const float4*>(g.ws + col) + 1);
+        p.b[j] = g.bias ? __ldg(reinterpret_cast<const uint4*>(g.bias + col)) : make_uint4(0, 0, 0, 0);
+        p.gt[j] = gate_row ? __ldg(reinterpret_cast<const uint4*>(gate_row + col)) : make_uint4(0, 0, 0, 0);
     }
+}
+
+// The dequant of one chunk runs on fp32 pairs: v = fp32(acc) * as * ws (two roundings, as the scalar form), + bias,
+// then fp16; the residual fp16(R + fp16(G * y)) uses fp16 pair operations, which round exactly like the fp32 form
+// (fp32 holds the exact sum or product of two fp16 values to within a rounding that cannot move the fp16 result).
+// The parameters of chunk c + 1 load while chunk c computes.
+template <int NCH>
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorMap* tmC, const CUtensorMap* tmR,
+                                              EpiCtx& e, uint32_t taddr, int row0, int n0, volatile int* abort) {
+    const int lane = threadIdx.x & 31;
+    const int m = row0 + lane;
+    const bool row_ok = m < g.M;
+    const uint64_t sa2 = splat2(row_ok ? g.as[m] : 0.f);
+    const int nc = min(NCH, (g.N - n0 + 31) / 32);
+    const bool res = g.R != nullptr;
+    const __half* gate_row = (res && row_ok) ? g.G + (int64_t)(m / g.L) * g.N : nullptr;
+    const int sw = (lane >> 1) & 3;
+    bool ok = true;
+    EpiParams P[2];
+    epi_params(g, gate_row, n0, P[0]);
+    if (res && lane == 0) {
+        bulk_wait_read<EPI_BUFS - 1>();
+        epi_load_r(tmR, e, e.n, n0, row0);
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        if (c >= nc) break;
+        EpiParams& p = P[c & 1];
+        if (c + 1 < nc) epi_params(g, gate_row, n0 + 32 * (c + 1), P[(c + 1) & 1]);
+        const uint32_t b = e.n % EPI_BUFS;
+        unsigned char* box = e.buf + b * EPI_BUF_BYTES;
+        if (res) {
+            if (lane == 0 && c + 1 < nc) {
+                bulk_wait_read<EPI_BUFS - 2>();
+                epi_load_r(tmR, e, e.n + 1, n0 + 32 * (c + 1), row0);
+            }
+            if (!mbar_wait(&e.rbar[b], (e.n / EPI_BUFS) & 1, abort, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) e.inflight &= ~(1u << b);
+        } else {
+            if (lane == 0) bulk_wait_read<EPI_BUFS - 1>();
+            __syncwarp();
+        }
+        uint32_t r[32];
+        tmem_ld32_wait(taddr + 32 * c, r);
+        unsigned char* row = box + lane * 64;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float* wv = reinterpret_cast<const float*>(&p.w[2 * j]);
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&p.b[j]);
+            const uint32_t* gw = reinterpret_cast<const uint32_t*>(&p.gt[j]);
+            uint4* slot = reinterpret_cast<uint4*>(row + ((j ^ sw) << 4));
+            uint4 rr = make_uint4(0, 0, 0, 0);
+            if (res) rr = *slot;
+            const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rr);
+            uint4 o;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint64_t v = mul2(mul2(pk2((float)(int32_t)r[8 * j + 2 * q], (float)(int32_t)r[8 * j + 2 * q + 1]), sa2),
+                                  pk2(wv[2 * q], wv[2 * q + 1]));
+                if (g.bias) {
+                    // Scalar adds: a packed add after the packed multiply was fused into one rounding by the
+                    // compiler, which moved some results by an fp16 step.
+                    const float2 f = upk2(v), bf = upk2(h2_to_f2(bw[q]));
+                    v = pk2(__fadd_rn(f.x, bf.x), __fadd_rn(f.y, bf.y));
+                }
+                uint32_t y = f2_to_h2(v);
+                if (res) y = h2_as_u32(__hadd2_rn(u32_as_h2(rw[q]), __hmul2_rn(u32_as_h2(gw[q]), u32_as_h2(y))));
+                ow[q] = y;
+            }
+            *slot = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(tmC, box, n0 + 32 * c, row0);
+            bulk_commit();
+        }
+        ++e.n;
+    }
+    if (!ok && lane == 0) epi_drain(e);
+    return ok;
 }
 
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+    gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, const GemmArgs g) {
     using C_ = Cfg<BN>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::STAGES * C_::STAGE_BYTES);
+    unsigned char* staging = smem + C_::STAGES * C_::STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + EPI_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + C_::STAGES;
     uint64_t* tfull = bars + 2 * C_::STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rbars = drain + 1;  // [4][EPI_BUFS]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 4 * EPI_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,6 +230,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(&tempty[a], 128);
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < 4 * EPI_BUFS; ++i) mbar_init(&rbars[i], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -231,6 +327,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else {
         const int quarter = warp & 3;
         const int row_local = quarter * 32 + lane;
+        EpiCtx e{staging + quarter * EPI_WARP_BYTES, rbars + quarter * EPI_BUFS, 0u, 0u};
         int it = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
             const int acc = it & 1;
@@ -238,15 +335,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
             tc_fence_after();
             const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
-            const int m = m0 + row_local;
-            const bool row_ok = m < g.M;
-            const float sa = (row_ok && g.as) ? g.as[m] : 0.f;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+            bool ok = true;
+            if (g.C32) {
+                const int m = m0 + row_local;
+                const bool row_ok = m < g.M;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) epilogue_chunk(g, taddr + c * 32, m, row_ok, sa, n0 + c * 32);
+                for (int c = 0; c < BN / 32; ++c) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+            } else {
+                ok = epilogue_tile<BN / 32>(g, &tmC, &tmR, e, taddr, m0 + quarter * 32, n0, abort_flag);
+            }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+            if (!ok) break;
         }
+        if (lane == 0) bulk_wait<0>();
     }
 
     tc_fence_before();
@@ -266,19 +369,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 constexpr int PAIR_STAGES = 6;
 constexpr int PAIR_HALF = 128 * BK;                    // 16 KB: 128 rows x 128 bytes
 constexpr int PAIR_STAGE_BYTES = 2 * PAIR_HALF;        // A half + B half
-constexpr int PAIR_SMEM = PAIR_STAGES * PAIR_STAGE_BYTES + 256 + 1024;
+constexpr int PAIR_SMEM = PAIR_STAGES * PAIR_STAGE_BYTES + EPI_BYTES + 512 + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
-    gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+    gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+                          const GemmArgs g) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PAIR_STAGES * PAIR_STAGE_BYTES);
+    unsigned char* staging = smem + PAIR_STAGES * PAIR_STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + EPI_BYTES);
     uint64_t* full = bars;                      // [STAGES] (CTA 0)
     uint64_t* empty = bars + PAIR_STAGES;       // [STAGES] (each CTA)
     uint64_t* tfull = bars + 2 * PAIR_STAGES;   // [2] (each CTA)
     uint64_t* tempty = tfull + 2;               // [2] (CTA 0)
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* rbars = drain + 1;                // [4][EPI_BUFS] (each CTA)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 4 * EPI_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -298,6 +405,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             mbar_init(&tempty[a], 8);  // one arrival per epilogue warp of each CTA
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < 4 * EPI_BUFS; ++i) mbar_init(&rbars[i], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -392,6 +500,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         const int quarter = warp & 3;
         const int row_local = quarter * 32 + lane;
         const uint32_t tempty0 = map_to_rank(smem_u32(tempty), 0);
+        EpiCtx e{staging + quarter * EPI_WARP_BYTES, rbars + quarter * EPI_BUFS, 0u, 0u};
         int it = 0;
         for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
             const int acc = it & 1;
@@ -399,16 +508,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
             tc_fence_after();
             const int m0 = (tile % num_m) * 256, n0 = (tile / num_m) * 256;
-            const int m = m0 + 128 * rank + row_local;
-            const bool row_ok = m < g.M;
-            const float sa = (row_ok && g.as) ? g.as[m] : 0.f;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
+            bool ok = true;
+            if (g.C32) {
+                const int m = m0 + 128 * rank + row_local;
+                const bool row_ok = m < g.M;
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) epilogue_chunk(g, taddr + c * 32, m, row_ok, sa, n0 + c * 32);
+                for (int c = 0; c < 8; ++c) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+            } else {
+                ok = epilogue_tile<8>(g, &tmC, &tmR, e, taddr, m0 + 128 * rank + quarter * 32, n0, abort_flag);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tempty0 + acc * 8);
+            if (!ok) break;
         }
+        if (lane == 0) bulk_wait<0>();
     }
 
     tc_fence_before();
@@ -418,10 +533,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
+// Output (and residual) maps: fp16 [M, N] row-major, 32 x 32 boxes with the 64-byte swizzle of the staging boxes.
+// The raw int32 path stores from registers and gets the A map as a placeholder.
+int make_out_maps(const GemmArgs& g, const CUtensorMap& fallback, CUtensorMap* tc, CUtensorMap* tr) {
+    *tc = fallback;
+    *tr = fallback;
+    if (g.C32) return B2_OK;
+    if (int rc = make_map_2d(tc, g.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.N, g.M, (uint64_t)g.N * 2, 32, 32,
+                             CU_TENSOR_MAP_SWIZZLE_64B))
+        return rc;
+    if (g.R)
+        if (int rc = make_map_2d(tr, g.R, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.N, g.M, (uint64_t)g.N * 2, 32, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_64B))
+            return rc;
+    return B2_OK;
+}
+
 int launch_pair(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_t stream) {
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tc, tr;
     if (int rc = make_map_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.M, g.K, BK, 128)) return rc;
     if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.K, BK, 128)) return rc;
+    if (int rc = make_out_maps(g, ta, &tc, &tr)) return rc;
     static int clusters[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -440,15 +572,16 @@ int launch_pair(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_
     }
     const int tiles = ((g.M + 255) / 256) * ((g.N + 255) / 256);
     const int nc = tiles < clusters[dev] ? tiles : clusters[dev];
-    gemm_w8a8_pair_kernel<<<2 * nc, GEMM_THREADS, PAIR_SMEM, stream>>>(ta, tb, g);
+    gemm_w8a8_pair_kernel<<<2 * nc, GEMM_THREADS, PAIR_SMEM, stream>>>(ta, tb, tc, tr, g);
     return check_launch("gemm_w8a8_pair_kernel");
 }
 
 template <int BN>
 int launch_bn(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_t stream) {
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tc, tr;
     if (int rc = make_map_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.M, g.K, BK, BM)) return rc;
     if (int rc = make_map_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.K, BK, BN)) return rc;
+    if (int rc = make_out_maps(g, ta, &tc, &tr)) return rc;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -458,7 +591,7 @@ int launch_bn(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_t 
     }
     const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_w8a8_kernel<BN><<<grid, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, g);
+    gemm_w8a8_kernel<BN><<<grid, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, tc, tr, g);
     return check_launch("gemm_w8a8_kernel");
 }
 

@@ -179,16 +179,6 @@ __device__ __forceinline__ int quant1(float f, float scale, float inv) {
 constexpr int R128_WARP_BYTES = 4096 + 1024;
 constexpr int R128_MAX_WARPS = MAX_K / 1024;
 
-__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ uint64_t h2_to_f2(uint32_t h) {
-    const float2 f = __half22float2(u32_as_h2(h));
-    return pk2(f.x, f.y);
-}
-__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
-    const float2 f = upk2(v);
-    return h2_as_u32(__floats2half2_rn(f.x, f.y));
-}
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
