@@ -22,7 +22,7 @@ __device__ unsigned int g_status;
 constexpr int TQ = 128;   // query rows per tile; a CTA computes two tiles (A and B) of one (batch, head)
 constexpr int TK = 128;   // keys per tile
 constexpr int HD = 128;   // head dim
-constexpr int ATT_THREADS = 320;
+constexpr int ATT_THREADS = 576;  // TMA warp, MMA warp, 16 softmax warps
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <bool I8>
@@ -35,7 +35,9 @@ struct AttCfg {
     static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
     static constexpr int OFF_KS = OFF_V + 2 * V_BYTES;
-    static constexpr int OFF_BAR = OFF_KS + 2 * KS_BYTES;
+    static constexpr int OFF_RED = OFF_KS + 2 * KS_BYTES;  // row max halves [parity][tile][row][half], l halves
+    static constexpr int RED_BYTES = 2 * 2 * TQ * 2 * 4 + 2 * TQ * 2 * 4;
+    static constexpr int OFF_BAR = OFF_RED + RED_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
 };
 
@@ -53,15 +55,26 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Meeting point of the two softmax warps that share 32 rows: an mbarrier of count 2 (one arrival per warp after
+// __syncwarp, so the warp's shared-memory writes are ordered before it), waited with the bounded wait.
+__device__ __forceinline__ bool pair_sync(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    return mbar_wait(bar, parity, abort, &g_status, B2_DEV_TIMEOUT_EPILOGUE);
+}
+
 // One CTA: 2 x 128 query rows of one (batch, head).
 //   warp 0      TMA: both Q tiles once, then K/V tiles of 128 keys into a 2-deep ring
 //   warp 1      TMEM owner and single-thread tcgen05.mma issuer. TMEM columns: S_A [0,128), S_B [128,256),
 //               O_A [256,384), O_B [384,512). Issue order per key tile j:
 //                 PV_A(j-1) ... S_A(j) ... PV_B(j-1) ... S_B(j)
 //               so the softmax of tile A on S_A(j) overlaps the tensor work for tile B and vice versa.
-//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B: thread = query row = TMEM lane. Two passes over S
-//               (row max, then p = exp2), P written back as fp16 into the consumed S columns, where the PV MMA
-//               reads it as its A operand (TMEM); lazy, warp-uniform rescale of O in TMEM.
+//   warps 2..9  softmax of tile A, warps 10..17 softmax of tile B. A warp owns 32 query rows (its TMEM lane
+//               quarter, thread = row) and one half of the 128 key columns; its partner (4 warps away) owns the
+//               other half of the same rows. Two passes over the half (row max, then p = exp2); the two halves'
+//               maxima meet through shared memory and a 64-thread barrier, so both take the same rescale decision.
+//               P is written back as fp16 into the half's consumed S columns, where the PV MMA reads it as its A
+//               operand (TMEM); lazy, warp-uniform rescale of the half's O columns in TMEM.
 template <bool I8>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -80,6 +93,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     uint64_t* o_done = bars + 13;  // [2]
     uint64_t* drain = bars + 15;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* pair_bar = bars + 17;  // [2 tiles][4 quarters]
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -96,13 +110,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             mbar_init(&k_full[i], 1);
             mbar_init(&v_full[i], 1);
             // int8: the key scales in the K stage are read by both softmax warpgroups too.
-            mbar_init(&k_empty[i], I8 ? 1 + 256 : 1);
+            mbar_init(&k_empty[i], I8 ? 1 + 16 : 1);  // MMA commit (+ one arrival per softmax warp)
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&p_full[i], 8);  // one arrival per softmax warp of the tile
             mbar_init(&o_done[i], 1);
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&pair_bar[i], 2);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -210,7 +225,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 const uint32_t v_addr = smem_u32(sV + (j & 1) * C_::V_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_f16_ts(tmem + 256 + t * HD, tmem + t * TK + kk * 8, sdesc_sw128(v_addr + kk * 2048, TK * 128, 1024),
+                    // P of keys [64 h, 64 h + 64) sits in columns [64 h, 64 h + 32) of the tile's S region
+                    mma_f16_ts(tmem + 256 + t * HD, tmem + t * TK + 64 * (kk >> 2) + 8 * (kk & 3),
+                               sdesc_sw128(v_addr + kk * 2048, TK * 128, 1024),
                                idesc_pv, (j | kk) != 0);
                 tc_commit(&o_done[t]);
             };
@@ -248,14 +265,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
         }
     } else {
-        // Softmax warpgroups: t = 0 (warps 2..5) or 1 (warps 6..9); thread -> query row r of tile t, TMEM lane r.
-        const int t = (warp - 2) >> 2;
+        // Softmax: tile t, key half hh, lane quarter (TMEM lanes 32 quarter .. + 31); thread -> query row r.
+        const int sw = warp - 2;
+        const int t = sw >> 3, hh = (sw >> 2) & 1;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
+        uint64_t* pbar = &pair_bar[t * 4 + quarter];
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        const uint32_t tS = tmem + lane_base + t * TK;
-        const uint32_t tO = tmem + lane_base + 256 + t * HD;
+        const uint32_t tS = tmem + lane_base + t * TK + 64 * hh;  // this half's 64 score columns
+        const uint32_t tO = tmem + lane_base + 256 + t * HD + 64 * hh;  // this half's 64 output columns
         const int qrow = q0 + t * TQ + r;
+        float* red = reinterpret_cast<float*>(smem + C_::OFF_RED);  // [2][2][TQ][2] maxima, then [2][TQ][2] sums
         float m = -1e30f, l = 0.f;
         float qs_c = 0.f;
         if (I8) qs_c = __fmul_rn(a.qscale[(int64_t)bh * a.Lq + min(qrow, a.Lq - 1)], a.scale_log2);
@@ -266,40 +286,55 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const int valid = a.Lk - j * TK;
-            const float* ks = sKS + (j & 1) * TK;
-            // Pass 1: row max of the scores (log2 domain). int8 scores are exact small integers (|dot| < 2^22) and
-            // become fp32 without the conversion pipe. TMEM is read in 32-column pieces so that the destination
-            // registers of tcgen05.ld never need to spill before tcgen05.wait::ld.
-            const bool full = valid >= TK;
-            float mx = -1e30f;
+            const int valid = a.Lk - j * TK - 64 * hh;  // valid keys of this half (may be <= 0 or >= 64)
+            const float* ks = sKS + (j & 1) * TK + 64 * hh;
+            const bool full = valid >= 64;
+            // Pass 1: the half's row max, four independent chains. int8 scores are exact small integers
+            // (|dot| < 2^22) that become fp32 without the conversion pipe and are scaled by q_scale * c and
+            // k_scale (hip_attention.hip:238-246); they go back to TMEM as fp32 for pass 2. fp16 scores enter the
+            // log2 domain after the max (the scale is applied to the max).
+            float mm[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t v[32];
                 tmem_ld32_wait(tS + c * 32, v);
-                float x[32];
+                if (I8) {
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    if (I8) {
+                    for (int i = 0; i < 32; i += 2) {
                         const float2 k2 = *reinterpret_cast<const float2*>(ks + c * 32 + i);
                         const float2 y = upk2(mul2(mul2(pk2(small_i2f(v[i]), small_i2f(v[i + 1])), pk2(qs_c, qs_c)),
                                                    pk2(k2.x, k2.y)));
-                        x[i] = y.x;
-                        x[i + 1] = y.y;
-                    } else {
-                        x[i] = __uint_as_float(v[i]);
-                        x[i + 1] = __uint_as_float(v[i + 1]);
+                        v[i] = __float_as_uint(y.x);
+                        v[i + 1] = __float_as_uint(y.y);
                     }
+                    tmem_st32(tS + c * 32, v);
                 }
                 if (full) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) mx = max3(mx, x[i], x[i + 1]);
+                    for (int i = 0; i < 32; i += 8)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            mm[q] = max3(mm[q], __uint_as_float(v[i + 2 * q]), __uint_as_float(v[i + 2 * q + 1]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c * 32 + i < valid) mx = fmaxf(mx, x[i]);
+                        if (c * 32 + i < valid) mm[i & 3] = fmaxf(mm[i & 3], __uint_as_float(v[i]));
                 }
             }
+            if (I8) {
+                tmem_wait_st();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&k_empty[j & 1]);  // the key scales of this stage are consumed
+            }
+            // The two halves' maxima meet (slot by tile parity, so a fast warp never overwrites a slot its partner
+            // still reads).
+            float* rm = red + (((j & 1) * 2 + t) * TQ + r) * 2;
+            rm[hh] = max3(mm[0], mm[1], fmaxf(mm[2], mm[3]));
+            if (!pair_sync(pbar, j & 1, abort_flag)) {
+                ok = false;
+                break;
+            }
+            float mx = fmaxf(rm[0], rm[1]);
             if (!I8) mx *= a.scale_log2;
             if (__any_sync(0xffffffffu, mx > m + 8.f)) {
                 const float mn = fmaxf(m, mx);
@@ -314,7 +349,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     }
                     tc_fence_after();
 #pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < 2; ++c) {
                         uint32_t o[32];
                         tmem_ld32_wait(tO + c * 32, o);
 #pragma unroll
@@ -323,29 +358,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                     }
                 }
             }
-            // Pass 2: p = exp2(s*c - m) (fp16 path) or exp2(s - m) (int8), l sums the fp32 p (two running partial
-            // sums), P (fp16 pairs) goes into the columns of S already consumed: 32 scores -> columns [16c, 16c + 16).
+            // Pass 2: p = exp2(s*c - m) (fp16 path) or exp2(s - m) (int8); l sums the fp32 p (two running partial
+            // sums); P (fp16 pairs) goes into the half's columns already read: 32 scores -> columns [16c, 16c + 16).
             const uint64_t c2 = I8 ? pk2(1.f, 1.f) : pk2(a.scale_log2, a.scale_log2);
             const uint64_t nm2 = pk2(-m, -m);
             uint64_t l2 = pk2(0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t v[32], pk[16];
                 tmem_ld32_wait(tS + c * 32, v);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    uint64_t s2;
-                    if (I8) {
-                        const float2 k2 = *reinterpret_cast<const float2*>(ks + c * 32 + 2 * i);
-                        s2 = mul2(mul2(pk2(small_i2f(v[2 * i]), small_i2f(v[2 * i + 1])), pk2(qs_c, qs_c)), pk2(k2.x, k2.y));
-                    } else {
-                        s2 = pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-                    }
-                    const float2 e = upk2(fma2(s2, c2, nm2));
+                    const int col = c * 32 + 2 * i;
+                    const float2 e = upk2(fma2(pk2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), c2, nm2));
                     float p0 = ex2(e.x), p1 = ex2(e.y);
                     if (!full) {
-                        if (c * 32 + 2 * i >= valid) p0 = 0.f;
-                        if (c * 32 + 2 * i + 1 >= valid) p1 = 0.f;
+                        if (col >= valid) p0 = 0.f;
+                        if (col + 1 >= valid) p1 = 0.f;
                     }
                     l2 = add2(l2, pk2(p0, p1));
                     const __half2 hp = __floats2half2_rn(p0, p1);
@@ -357,18 +386,25 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 const float2 lf = upk2(l2);
                 l += lf.x + lf.y;
             }
-            if (I8) mbar_arrive(&k_empty[j & 1]);  // key scales of this stage are consumed
+            // Every lane's P stores complete before the warp's single arrival (serialized arrivals of 256 threads on
+            // one barrier cost more than the whole handshake otherwise).
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[t]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
+        // The row sum is the two halves' sums (half 0 first in both warps, so both use the same l).
+        float* rl = red + 2 * 2 * TQ * 2 + (t * TQ + r) * 2;
+        rl[hh] = l;
+        if (ok) ok = pair_sync(pbar, n_tiles & 1, abort_flag);
+        l = rl[0] + rl[1];
         if (ok && mbar_wait(&o_done[t], (n_tiles - 1) & 1, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
             tc_fence_after();
             const float inv = 1.f / l;
             const bool row_ok = qrow < a.Lq;
-            __half* dst = a.out + (int64_t)b * a.sob + (int64_t)h * a.soh + (int64_t)qrow * a.sol;
+            __half* dst = a.out + (int64_t)b * a.sob + (int64_t)h * a.soh + (int64_t)qrow * a.sol + 64 * hh;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t o[32];
                 tmem_ld32_wait(tO + c * 32, o);
                 if (row_ok) {
