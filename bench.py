@@ -136,18 +136,26 @@ def max_over_ranks(x, world):
     return x
 
 
-def timed(run_step, steps, warmup, world, kernel_events=None):
+def timed(run_step, steps, warmup, world, begin=None, finish=None):
     """W warm-up steps, then K steps between a barrier + synchronize on both sides; CUDA events on the current
-    stream. Returns (total ms over the K steps, max over ranks)."""
+    stream. ``begin`` runs right after the start event (a pipelined step restarts there, so that every timed step's
+    copies happen after it), ``finish`` right before the end event (it makes the current stream wait for work
+    that the steps left on other streams). Returns the total ms over the K steps, max over ranks."""
     for i in range(warmup):
         run_step(i)
+    if finish:
+        finish()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
+    if begin:
+        begin()
     for i in range(steps):
         run_step(warmup + i)
+    if finish:
+        finish()
     end.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -672,10 +680,41 @@ class DiTC4:
                 self.events = [(None, None)]
                 self.gemm_ms, self.gemm_ops = g["ms"], g["work"]
 
+    def e2e_begin(self):
+        if not hasattr(self, "copy_stream"):
+            self.copy_stream = torch.cuda.Stream()
+            self.xb = [torch.empty_like(self.x0), torch.empty_like(self.x0)]
+            self.in_ev = [torch.cuda.Event(), torch.cuda.Event()]
+            self.fwd_ev = [torch.cuda.Event(), torch.cuda.Event()]
+        self.prefetched = None
+
     def e2e_step(self, i):
-        self.x.copy_(self.x_host, non_blocking=True)
-        self.stack.forward(self.x)
-        self.out_host.copy_(self.x, non_blocking=True)
+        """One step through the public path with host buffers, pipelined the way a serving loop runs it: the step's
+        input arrives from pinned host memory on a copy stream (prefetched during the previous step, or fetched now
+        for the first step after e2e_begin), the forward runs in place, and the result goes back to pinned host
+        memory on the copy stream while the next step computes. The copy stream fetches the next step's input first,
+        then returns this step's output, so both transfers overlap compute and stay ordered with the buffer reuse."""
+        if not hasattr(self, "copy_stream"):
+            self.e2e_begin()
+        main, cs = torch.cuda.current_stream(), self.copy_stream
+        cur, nxt = i % 2, (i + 1) % 2
+        if self.prefetched != i:
+            cs.wait_stream(main)
+            with torch.cuda.stream(cs):
+                self.xb[cur].copy_(self.x_host, non_blocking=True)
+                self.in_ev[cur].record(cs)
+        main.wait_event(self.in_ev[cur])
+        self.stack.forward(self.xb[cur])
+        self.fwd_ev[cur].record(main)
+        with torch.cuda.stream(cs):
+            self.xb[nxt].copy_(self.x_host, non_blocking=True)  # buffer nxt: its previous output left earlier on cs
+            self.in_ev[nxt].record(cs)
+            cs.wait_event(self.fwd_ev[cur])
+            self.out_host.copy_(self.xb[cur], non_blocking=True)
+        self.prefetched = i + 1
+
+    def e2e_finish(self):
+        torch.cuda.current_stream().wait_stream(self.copy_stream)
 
     h2d_bytes = property(lambda self: self.x_host.numel() * 2)
     d2h_bytes = property(lambda self: self.x_host.numel() * 2)
@@ -816,7 +855,8 @@ def main():
             wl.step(i)
         torch.cuda.synchronize()
         ms = timed(wl.step, args.steps, args.warmup, world)
-    e2e_ms = timed(wl.e2e_step, args.steps, args.warmup, world)
+    e2e_ms = timed(wl.e2e_step, args.steps, args.warmup, world, begin=getattr(wl, "e2e_begin", None),
+                   finish=getattr(wl, "e2e_finish", None))
 
     line = {"metric": wl.metric, "value": wl.value(ms, args.steps, world), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
