@@ -34,12 +34,12 @@ L2_BYTES = 126 * 1024 * 1024
 # ncu capture of that kernel on a B200 (cold L2).  Output lines still dirty in L2 when a kernel ends are not counted
 # as written yet, so a kernel whose output fits in L2 can show less than its algorithmic bytes.
 NCU_TRAFFIC = {
-    "attn": 149.61e6 + 29.04e6,      # C2 fp16, one launch
+    "attn": 149.87e6 + 31.14e6,      # C2 fp16, one launch
     "attn_i8": 101.35e6 + 23.09e6,   # C2 int8 QK, one launch
     "w4a8": 22.17e6 + 0.60e6,        # C3, one launch
-    "prepass": 40.86e6 + 0.25e6,     # C4 QKV pre-pass (MOD), one launch; the 20.4 MB int8 output stays in L2
+    "prepass": 40.87e6 + 0.46e6,     # C4 QKV pre-pass (MOD), one launch; the 20.4 MB int8 output stays in L2
     "decode": 15.78e6 * 19456 / 6144,  # captured on the 6144-row qkv GEMV; bytes grow with rows (2568 B per row)
-    "dit": 112.50e6 + 69.24e6,       # mean over the 32 W8A8 GEMM launches of one DiT step
+    "dit": 115.8e6 + 78.2e6,         # mean over the 32 W8A8 GEMM launches of one DiT step
 }
 
 
@@ -487,7 +487,7 @@ class PrepassC4:
     def roofline(self, peaks, kms):
         achieved = self.bytes / (kms * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["prepass"], "kernel": "prepass_kernel<MOD,128>",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["prepass"], "kernel": "prepass128_kernel<MOD>",
                 "note": f"{peaks['source']} HBM copy bandwidth"}
 
     @staticmethod
