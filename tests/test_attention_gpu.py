@@ -111,3 +111,24 @@ def test_config2_full_size(pkg, dev, int8_qk):
             den += ref.pow(2).sum().item()
     assert (num / den) ** 0.5 < (1e-2 if int8_qk else 2e-3)
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("B,H,Hkv,Lq,Lk", [(2, 12, 12, 3321, 3321), (1, 40, 8, 1300, 1000), (1, 80, 80, 600, 70)])
+def test_full_grid_shapes(pkg, dev, B, H, Hkv, Lq, Lk):
+    """Grids of more than one CTA per SM: the DiT's 3321-row sequences (the last CTA's second tile partly past Lq),
+    grouped-query heads and a partial key tile; checked against fp32 torch on a few heads."""
+    gen = torch.Generator(device="cpu").manual_seed(B * 1000 + H)
+    q = torch.randn((B, H, Lq, 128), generator=gen).half().to(dev)
+    k, v = (torch.randn((B, Hkv, Lk, 128), generator=gen).half().to(dev) for _ in range(2))
+    out = torch.full_like(q, float("nan"))
+    pkg.ops.attention(q, k, v, out, 128 ** -0.5)
+    assert torch.isfinite(out).all()
+    num = den = 0.0
+    rep = H // Hkv
+    for b in range(B):
+        for h in sorted({0, H // 2, H - 1}):
+            s = (q[b, h].float() @ k[b, h // rep].float().t()) * 128 ** -0.5
+            ref = torch.softmax(s, -1) @ v[b, h // rep].float()
+            num += (out[b, h].float() - ref).pow(2).sum().item()
+            den += ref.pow(2).sum().item()
+    assert (num / den) ** 0.5 < 2e-3
