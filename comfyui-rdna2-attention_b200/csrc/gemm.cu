@@ -5,12 +5,13 @@
 //   y = (float)acc * as[m] * ws[n] (+ (float)bias[n]) -> fp16
 //   residual: out = fp16(R[m,n] + fp16(G[m / L, n] * y))
 //
-// Structure: a persistent kernel, one CTA per SM, 6 warps.
+// Structure: a persistent kernel, one CTA per SM, 6 warps; tiles 128 x BN (BN = 128, 192 or 256, whichever needs the
+// fewest waves x width) or, for large problems, 256 x 256 on CTA pairs (gemm_w8a8_pair_kernel below).
 //   warp 0      TMA producer: 128x128 A tiles and BNx128 B tiles (128-byte swizzle) into a STAGES-deep ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=BN, K=32 per instruction)
 //   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (each warp its 32-lane quarter), dequant,
 //               bias, residual, fp16 through a swizzled shared-memory box and one TMA store per 32 x 32 box
-// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the main loop of tile i+1.
+// Two TMEM accumulators (BN columns each) let the epilogue of tile i overlap the main loop of tile i+1.
 #include "common.cuh"
 #include "host.hpp"
 
@@ -31,11 +32,12 @@ constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 
 template <int BN>
 struct Cfg {
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int STAGES = BN == 256 ? 4 : BN == 192 ? 5 : 6;
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int ACC_STRIDE = BN == 192 ? 256 : BN;  // TMEM columns between the two accumulators
+    static constexpr int TMEM_COLS = 2 * ACC_STRIDE;          // allocations are powers of two
     static constexpr int BAR_BYTES = 512;
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;
 };
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * BN;
+                const uint32_t d_tmem = tmem_base + acc * C_::ACC_STRIDE;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, &g_status, B2_DEV_TIMEOUT_MMA)) {
                         ok = false;
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
             tc_fence_after();
             const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
-            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * C_::ACC_STRIDE;
             bool ok = true;
             if (g.C32) {
                 const int m = m0 + row_local;
@@ -603,10 +605,16 @@ int run(const int8_t* A, const int8_t* B, GemmArgs& g, cudaStream_t stream) {
     if (!aligned16(A) || !aligned16(B)) return fail(B2_ERR_UNSUPPORTED, "gemm: A and B must be 16-byte aligned");
     if (g.M == 0) return B2_OK;
     // CTA pairs on 256 x 256 tiles when they fill the machine; single-CTA tiles for small problems.
-    const int tiles256 = ((g.M + BM - 1) / BM) * ((g.N + 255) / 256);
+    // Otherwise the tile width with the least estimated time: waves of single-CTA tiles x tile width.
+    auto cost = [&](int bn) {
+        const int64_t tiles = (int64_t)((g.M + BM - 1) / BM) * ((g.N + bn - 1) / bn);
+        return ((tiles + sm_count() - 1) / sm_count()) * bn;
+    };
     if (g.M >= 256 && g.N >= 256 && ((g.M + 255) / 256) * ((g.N + 255) / 256) >= sm_count() / 2)
         return launch_pair(A, B, g, stream);
-    if (tiles256 >= sm_count()) return launch_bn<256>(A, B, g, stream);
+    const int64_t c128 = cost(128), c192 = cost(192), c256 = cost(256);
+    if (c256 <= c192 && c256 <= c128) return launch_bn<256>(A, B, g, stream);
+    if (c192 < c128) return launch_bn<192>(A, B, g, stream);
     return launch_bn<128>(A, B, g, stream);
 }
 

@@ -45,7 +45,8 @@ def test_int32_extremes(pkg, dev):
     assert np.array_equal(got, ogemm.int_mm(a, b))
 
 
-@pytest.mark.parametrize("M,N,K", [(77, 264, 384), (1024, 3072, 3072), (513, 128, 8192), (2049, 2568, 512)])
+@pytest.mark.parametrize("M,N,K", [(77, 264, 384), (1024, 3072, 3072), (513, 128, 8192), (2049, 2568, 512),
+                                   (1100, 2600, 384)])
 def test_epilogue_bit_exact(pkg, dev, M, N, K):
     g = np.random.default_rng(M)
     a, b = rand_i8((M, K), 1), rand_i8((N, K), 2)
