@@ -29,6 +29,7 @@ SIGNATURES = {
     "b2_mod_quant_pack_a": (I, [P, I64, P, P, P, I, F, P, P, I, I, I, P, P]),
     "b2_gemm": (I, [P, P, P, P, P, P, I, I, I, P, P, I, P]),
     "b2_gemm_i32": (I, [P, P, P, I, I, I, P]),
+    "b2_gemm_swiglu": (I, [P, P, P, P, P, I, I, I, P]),
     "b2_gemm_w4a8": (I, [P, P, P, P, P, P, I, I, I, P]),
     "b2_attention_workspace_bytes": (I64, [I, I, I, I, I, I]),
     "b2_attention": (I, [P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64,

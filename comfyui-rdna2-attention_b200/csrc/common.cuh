@@ -425,6 +425,30 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// 1 / (1 + exp(-g)) for a pair: exp(-g) = 2^(-g log2 e) with the hardware base-2 approximation, then the hardware
+// reciprocal approximation (a few fp32 ulps; the SwiGLU and gate activations round the result to fp16).
+__device__ __forceinline__ uint64_t sigmoid2(uint64_t G) {
+    const float2 m = upk2(mul2(G, splat2(-1.4426950408889634f)));
+    const float2 d = upk2(add2(pk2(ex2_approx(m.x), ex2_approx(m.y)), splat2(1.f)));
+    return pk2(rcp_approx(d.x), rcp_approx(d.y));
+}
+// SwiGLU of fp16 pairs: fp16(fp16(g sigmoid(g)) u); the product of two fp16 values rounded once is the fp32 path's.
+__device__ __forceinline__ uint32_t swiglu_h2(uint32_t g, uint32_t u) {
+    const float2 gf = __half22float2(u32_as_h2(g));
+    const uint64_t G = pk2(gf.x, gf.y);
+    const uint32_t silu = f2_to_h2(mul2(G, sigmoid2(G)));
+    return h2_as_u32(__hmul2_rn(u32_as_h2(silu), u32_as_h2(u)));
+}
 // int32 in (-2^22, 2^22) -> fp32, exact: the integer added to the bits of 1.5 * 2^23 lands in the mantissa.
 __device__ __forceinline__ float small_i2f(uint32_t v) {
     return __int_as_float((int)v + 0x4B400000) - 12582912.f;

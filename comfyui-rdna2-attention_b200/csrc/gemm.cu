@@ -52,6 +52,7 @@ struct GemmArgs {
     const __half* G;
     int L;
     int M, N, K;
+    int swiglu;  // gate/up GEMM with rows interleaved in blocks of 128: C[M, N/2] = SwiGLU(gate, up)
 };
 
 // 32 raw int32 accumulator columns of one row (the debugging output C32), stored from registers.
@@ -199,6 +200,67 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
     return ok;
 }
 
+// SwiGLU epilogue of a 256-wide tile whose weight rows hold gate features [f, f + 128) in columns 0..127 and the
+// matching up features in columns 128..255 (rows interleaved in blocks of 128). Output chunk oc (32 features) pairs
+// accumulator columns 32 oc (gate) and 128 + 32 oc (up): g and u are the epilogue's fp16 values, then
+// fp16(fp16(g sigmoid(g)) u) with the same arithmetic as the pre-pass's SwiGLU, written as one 32 x 32 box of
+// C[M, N/2] at feature column n0 / 2 + 32 oc. A chunk's per-column scales load while its TMEM columns are read.
+struct SwiParams {
+    float4 wg[8], wu[8];
+};
+
+__device__ __forceinline__ void swi_params(const GemmArgs& g, int n0, int oc, SwiParams& p) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        p.wg[j] = __ldg(reinterpret_cast<const float4*>(g.ws + n0 + 32 * oc) + j);
+        p.wu[j] = __ldg(reinterpret_cast<const float4*>(g.ws + n0 + 128 + 32 * oc) + j);
+    }
+}
+
+__device__ __forceinline__ void epilogue_tile_swiglu(const GemmArgs& g, const CUtensorMap* tmC, EpiCtx& e,
+                                                     uint32_t taddr, int row0, int n0) {
+    const int lane = threadIdx.x & 31;
+    const int m = row0 + lane;
+    const uint64_t sa2 = splat2(m < g.M ? g.as[m] : 0.f);
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int oc = 0; oc < 4; ++oc) {
+        SwiParams p;
+        swi_params(g, n0, oc, p);
+        unsigned char* box = e.buf + (e.n % EPI_BUFS) * EPI_BUF_BYTES;
+        if (lane == 0) bulk_wait_read<EPI_BUFS - 1>();
+        __syncwarp();
+        uint32_t rg[32], ru[32];
+        tmem_ld32_wait(taddr + 32 * oc, rg);
+        tmem_ld32_wait(taddr + 128 + 32 * oc, ru);
+        const float* wg = reinterpret_cast<const float*>(p.wg);
+        const float* wu = reinterpret_cast<const float*>(p.wu);
+        unsigned char* row = box + lane * 64;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint4 o;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int i = 8 * j + 2 * q;
+                const uint32_t gh = f2_to_h2(mul2(mul2(pk2((float)(int32_t)rg[i], (float)(int32_t)rg[i + 1]), sa2),
+                                                  pk2(wg[i], wg[i + 1])));
+                const uint32_t uh = f2_to_h2(mul2(mul2(pk2((float)(int32_t)ru[i], (float)(int32_t)ru[i + 1]), sa2),
+                                                  pk2(wu[i], wu[i + 1])));
+                ow[q] = swiglu_h2(gh, uh);
+            }
+            *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(tmC, box, n0 / 2 + 32 * oc, row0);
+            bulk_commit();
+        }
+        ++e.n;
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -344,6 +406,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 const bool row_ok = m < g.M;
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; ++c) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+            } else if (BN == 256 && g.swiglu) {
+                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + quarter * 32, n0);
             } else {
                 ok = epilogue_tile<BN / 32>(g, &tmC, &tmR, e, taddr, m0 + quarter * 32, n0, abort_flag);
             }
@@ -517,6 +581,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 const bool row_ok = m < g.M;
 #pragma unroll 1
                 for (int c = 0; c < 8; ++c) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+            } else if (g.swiglu) {
+                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + 128 * rank + quarter * 32, n0);
             } else {
                 ok = epilogue_tile<8>(g, &tmC, &tmR, e, taddr, m0 + 128 * rank + quarter * 32, n0, abort_flag);
             }
@@ -541,7 +607,8 @@ int make_out_maps(const GemmArgs& g, const CUtensorMap& fallback, CUtensorMap* t
     *tc = fallback;
     *tr = fallback;
     if (g.C32) return B2_OK;
-    if (int rc = make_map_2d(tc, g.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.N, g.M, (uint64_t)g.N * 2, 32, 32,
+    const int nc = g.swiglu ? g.N / 2 : g.N;
+    if (int rc = make_map_2d(tc, g.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, nc, g.M, (uint64_t)nc * 2, 32, 32,
                              CU_TENSOR_MAP_SWIZZLE_64B))
         return rc;
     if (g.R)
@@ -612,6 +679,7 @@ int run(const int8_t* A, const int8_t* B, GemmArgs& g, cudaStream_t stream) {
     };
     if (g.M >= 256 && g.N >= 256 && ((g.M + 255) / 256) * ((g.N + 255) / 256) >= sm_count() / 2)
         return launch_pair(A, B, g, stream);
+    if (g.swiglu) return launch_bn<256>(A, B, g, stream);  // the SwiGLU epilogue pairs the two halves of 256 columns
     const int64_t c128 = cost(128), c192 = cost(192), c256 = cost(256);
     if (c256 <= c192 && c256 <= c128) return launch_bn<256>(A, B, g, stream);
     if (c192 < c128) return launch_bn<192>(A, B, g, stream);
@@ -648,6 +716,23 @@ extern "C" int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const 
     g.M = M;
     g.N = N;
     g.K = K;
+    return run(A, B, g, (cudaStream_t)stream);
+}
+
+extern "C" int b2_gemm_swiglu(const int8_t* A, const int8_t* B, const float* as, const float* ws, uint16_t* C, int M,
+                              int N, int K, void* stream) {
+    if (!as || !ws || !C) return fail(B2_ERR_INVALID, "gemm_swiglu: null scale or output");
+    if (N <= 0 || N % 256) return fail(B2_ERR_UNSUPPORTED, "gemm_swiglu: N=%d must be a multiple of 256", N);
+    if (!aligned16(C) || !aligned16(ws)) return fail(B2_ERR_UNSUPPORTED, "gemm_swiglu: C and ws must be 16-byte aligned");
+    GemmArgs g{};
+    g.as = as;
+    g.ws = ws;
+    g.C = reinterpret_cast<__half*>(C);
+    g.L = 1;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.swiglu = 1;
     return run(A, B, g, (cudaStream_t)stream);
 }
 

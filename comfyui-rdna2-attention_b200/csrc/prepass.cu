@@ -179,16 +179,6 @@ __device__ __forceinline__ int quant1(float f, float scale, float inv) {
 constexpr int R128_WARP_BYTES = 4096 + 1024;
 constexpr int R128_MAX_WARPS = MAX_K / 1024;
 
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 // max(a, |b|, |c|) with NaN propagation: any NaN operand gives NaN.
 __device__ __forceinline__ float max3_abs_nan(float a, float b, float c) {
     float d;
@@ -203,13 +193,6 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     return r;
 }
 
-// 1 / (1 + exp(-g)) for a pair: exp(-g) = 2^(-g log2 e) with the hardware base-2 approximation, then the hardware
-// reciprocal approximation (a few fp32 ulps, like the per-value silu_mul / sigmoid_gate above).
-__device__ __forceinline__ uint64_t sigmoid2(uint64_t G) {
-    const float2 m = upk2(mul2(G, splat2(-1.4426950408889634f)));
-    const float2 d = upk2(add2(pk2(ex2_approx(m.x), ex2_approx(m.y)), splat2(1.f)));
-    return pk2(rcp_approx(d.x), rcp_approx(d.y));
-}
 
 __device__ __forceinline__ void bfly2(uint64_t& a, uint64_t& b) {
     const uint64_t x = a, y = b;
@@ -313,10 +296,7 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
                     if (ACT == ACT_SWIGLU) {
-                        // fp16(fp16(g sigmoid(g)) u): a product of two fp16 values rounded once is the fp32 path's
-                        const uint64_t G = h2_to_f2(xw[p]);
-                        const uint32_t silu = f2_to_h2(mul2(G, sigmoid2(G)));
-                        y[o][p] = h2_as_u32(__hmul2_rn(u32_as_h2(silu), u32_as_h2(uw[p])));
+                        y[o][p] = swiglu_h2(xw[p], uw[p]);
                     } else if (ACT == ACT_GATE) {
                         const uint32_t sig = f2_to_h2(sigmoid2(h2_to_f2(uw[p])));
                         y[o][p] = h2_as_u32(__hmul2_rn(u32_as_h2(xw[p]), u32_as_h2(sig)));

@@ -5,7 +5,10 @@ rotate(RMSNorm(x))))), every linear W8A8 with per-channel int8 weights, block-12
 fp16 attention with 24 heads of 128. On the device one block is 9 launches:
   mod pre-pass (RMSNorm + rotation + int8) -> QKV GEMM -> attention (reads Q/K/V as strided views of the QKV
   output) -> pre-pass -> out-proj GEMM with the residual in its epilogue -> mod pre-pass -> gate|up GEMM (one
-  N = 2 x 8192 GEMM) -> SwiGLU pre-pass (reads gate and up in place) -> down GEMM with the residual.
+  N = 2 x 8192 GEMM whose epilogue applies the SwiGLU and writes the 8192-wide activation: its weight rows are
+  interleaved in blocks of 128) -> pre-pass -> down GEMM with the residual. The configuration fuses the SwiGLU into
+  the down projection's pre-pass; here it moves one kernel earlier, with the same fp16 arithmetic, which halves the
+  activation written to and read back from HBM.
 The reference's fused Krea-2 block (int8_gemm.py:189-226) has the same shape with modulation and gates; this is the
 configuration's simplified form.
 
@@ -114,7 +117,12 @@ class DiTBlock:
         rows = qkv_rows(cfg, plan.head_lo, plan.head_hi).to(device)
         self.w_qkv, self.s_qkv = w_qkv.index_select(0, rows).contiguous(), s_qkv.index_select(0, rows).contiguous()
         self.w_o, self.s_o = weight(D, D)
-        self.w_gu, self.s_gu = weight(2 * F, D)
+        # Gate and up rows interleaved in blocks of 128 (gu_perm[i] = natural row of stored row i), so that the
+        # gate/up GEMM applies the SwiGLU in its epilogue.
+        w_gu, s_gu = weight(2 * F, D)
+        self.gu_perm = ops.swiglu_interleave(2 * F, device)
+        self.w_gu, self.s_gu = w_gu.index_select(0, self.gu_perm).contiguous(), s_gu.index_select(0, self.gu_perm).contiguous()
+        del w_gu, s_gu
         self.w_down, self.s_down = weight(D, F)
         self.norm1 = (torch.randn(D, generator=gen, device=device) * 0.02).float()
         self.norm2 = (torch.randn(D, generator=gen, device=device) * 0.02).float()
@@ -144,7 +152,7 @@ class DiTStack:
         self.att = torch.empty((b, cfg.tokens, hl, cfg.head_dim), dtype=torch.float16, device=dev)
         g = plan.group_size
         self.gathered = torch.empty((g, b, cfg.tokens, hl * cfg.head_dim), dtype=torch.float16, device=dev) if g > 1 else None
-        self.gu = torch.empty((M, 2 * F), dtype=torch.float16, device=dev)
+        self.act = torch.empty((M, F), dtype=torch.float16, device=dev)
         self.xa = torch.empty((M, D), dtype=torch.float16, device=dev)
 
     def attention_part(self, blk, x):
@@ -182,10 +190,10 @@ class DiTStack:
         with t("prepass"):
             ops.mod_quant_pack_a(self.xa, blk.norm2, self.ones, self.zeros, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
         with t("gemm", 2 * M * D * 2 * F):
-            ops.gemm(q8, self.sa, blk.w_gu, blk.s_gu, out=self.gu)
+            ops.gemm_swiglu(q8, self.sa, blk.w_gu, blk.s_gu, out=self.act)
         q8f = self.q8[:M * F].view(M, F)
         with t("prepass"):
-            ops.swiglu_quant_pack_a(self.gu[:, :F], self.gu[:, F:], cfg.rot_group, out=(q8f, self.sa))
+            ops.quant_pack_a(self.act, cfg.rot_group, out=(q8f, self.sa))
         with t("gemm", 2 * M * F * D):
             ops.gemm(q8f, self.sa, blk.w_down, blk.s_down, residual=self.xa, gate=self.ones, L=T, out=x2)
         return x

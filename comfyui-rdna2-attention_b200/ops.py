@@ -124,6 +124,36 @@ def gemm_i32(a_q, w_q):
     return out
 
 
+def swiglu_interleave(n2, device=None):
+    """Row order of a gate/up weight [2F, K] for gemm_swiglu: gate rows and up rows alternate in blocks of 128
+    (returns the natural row index of each interleaved row)."""
+    F = n2 // 2
+    if n2 % 256:
+        raise RuntimeError(f"gemm_swiglu needs 2F % 256 == 0 (got {n2})")
+    blk = torch.arange(F // 128).repeat_interleave(128) * 128 + torch.arange(128).repeat(F // 128)
+    idx = torch.stack((blk.view(-1, 128), (blk + F).view(-1, 128)), 1).reshape(-1)
+    return idx.to(device) if device is not None else idx
+
+
+def gemm_swiglu(a_q, a_scale, w_q, w_scale, out=None):
+    """fp16 [M, F] = SwiGLU(gate, up) of the gate/up projection, in the GEMM's epilogue. w_q int8 [2F, K] and
+    w_scale fp32 [2F] in the order of swiglu_interleave."""
+    require_cuda(a_q, a_scale, w_q, w_scale)
+    M, K = a_q.shape
+    N = w_q.shape[0]
+    if a_q.dtype != torch.int8 or w_q.dtype != torch.int8 or w_q.shape[1] != K:
+        raise RuntimeError("gemm_swiglu operands must be int8 [M, K] and [2F, K]")
+    if not (a_q.is_contiguous() and w_q.is_contiguous()):
+        raise RuntimeError("gemm_swiglu operands must be contiguous")
+    if a_scale.dtype != torch.float32 or w_scale.dtype != torch.float32:
+        raise RuntimeError("gemm_swiglu scales must be fp32")
+    if out is None:
+        out = torch.empty((M, N // 2), dtype=torch.float16, device=a_q.device)
+    call("b2_gemm_swiglu", ptr(a_q), ptr(w_q), ptr(a_scale), ptr(w_scale.contiguous()), ptr(out), I(M), I(N), I(K),
+         stream())
+    return out
+
+
 def w4a8_scales(scales_fp16):
     """fp16 group scales [N, K/128] -> the kernel's fp32 [K/128, N] (exact widening, done once per weight)."""
     return scales_fp16.to(torch.float32).t().contiguous()

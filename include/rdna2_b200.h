@@ -89,6 +89,15 @@ int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const float* ws, 
             int M, int N, int K, const uint16_t* R, const uint16_t* G, int L, void* stream);
 /* Raw int32 accumulators C32[M, N] = A B^T of the same kernel, for bit-exact checks. */
 int b2_gemm_i32(const int8_t* A, const int8_t* B, int32_t* C32, int M, int N, int K, void* stream);
+/* Gate/up projection with the SwiGLU applied in the epilogue (no counterpart entry point in the reference: its
+ * SwiGLU runs in the next layer's pre-pass, swiglu_rot_quant_pack_a, int8_gemm.hip:253, which this replaces for
+ * callers that own the weight layout). B's rows hold the gate and up weights interleaved in blocks of 128: rows
+ * [256 j, 256 j + 128) are gate features [128 j, 128 j + 128), rows [256 j + 128, 256 j + 256) the matching up
+ * features; ws is ordered the same way. C[M, N/2] = fp16(fp16(g sigmoid(g)) u) with g and u the fp16 epilogue
+ * values (as in b2_gemm without bias), the same SwiGLU arithmetic as b2_swiglu_quant_pack_a's act_out.
+ * Needs N % 256 == 0 and K % 16 == 0. */
+int b2_gemm_swiglu(const int8_t* A, const int8_t* B, const float* as, const float* ws, uint16_t* C, int M, int N,
+                   int K, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * W4A8 GEMM with group-128 weight scales (the configuration's tuned-int4 form). The reference's int4 path is

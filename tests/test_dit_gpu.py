@@ -51,7 +51,8 @@ def oracle_block(x, blk, cfg):
     q, s = quant(att)
     xa = ogemm.epilogue(ogemm.int_mm(q, cpu(blk.w_o)), s, cpu(blk.s_o), R=xf, G=ones, L=T)
     q, s = quant(oq.modulate(xa, cpu(blk.norm2), ones, zeros, T, cfg.eps))
-    gu = ogemm.epilogue(ogemm.int_mm(q, cpu(blk.w_gu)), s, cpu(blk.s_gu))
+    inv = np.argsort(cpu(blk.gu_perm))  # stored rows are gate/up interleaved in blocks of 128
+    gu = ogemm.epilogue(ogemm.int_mm(q, cpu(blk.w_gu)[inv]), s, cpu(blk.s_gu)[inv])
     q, s = quant(oq.swiglu(gu[:, :F], gu[:, F:]))
     return ogemm.epilogue(ogemm.int_mm(q, cpu(blk.w_down)), s, cpu(blk.s_down), R=xa, G=ones, L=T).reshape(B, T, D)
 

@@ -95,3 +95,21 @@ def test_config1_linear_end_to_end(pkg, dev, rot):
     exact = x.astype(np.float64) @ w.T.astype(np.float64) + bias.astype(np.float64)
     rel = np.linalg.norm(got.astype(np.float64) - exact) / np.linalg.norm(exact)
     assert rel < 3e-2  # W8A8 quantization error with outliers, for scale
+
+
+@pytest.mark.parametrize("M,F,K", [(300, 1024, 384), (2049, 2048, 512)])
+def test_swiglu_epilogue_matches_gemm_then_prepass(pkg, dev, M, F, K):
+    """The SwiGLU epilogue (gate/up rows interleaved in blocks of 128) equals the plain GEMM followed by the SwiGLU
+    pre-pass's activation bit for bit (F % 1024 == 0: the pre-pass kernel with the same SwiGLU arithmetic), on the
+    single-CTA (300 rows) and CTA-pair (2049 rows) kernels."""
+    a, b = rand_i8((M, K), 7), rand_i8((2 * F, K), 8)
+    g = np.random.default_rng(9)
+    sa = (g.random(M) * 0.05 + 1e-3).astype(F32)
+    sw = (g.random(2 * F) * 2e-3 + 1e-5).astype(F32)
+    A, Bw, SA, SW = dev_(a, dev), dev_(b, dev), dev_(sa, dev), dev_(sw, dev)
+    gu = pkg.ops.gemm(A, SA, Bw, SW)
+    act = torch.empty((M, F), dtype=torch.float16, device=dev)
+    pkg.ops.swiglu_quant_pack_a(gu[:, :F].contiguous(), gu[:, F:].contiguous(), 128, act_out=act)
+    perm = pkg.ops.swiglu_interleave(2 * F, dev)
+    fused = pkg.ops.gemm_swiglu(A, SA, Bw.index_select(0, perm).contiguous(), SW.index_select(0, perm).contiguous())
+    assert torch.equal(fused, act)
