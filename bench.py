@@ -39,7 +39,7 @@ NCU_TRAFFIC = {
     "w4a8": 22.17e6 + 0.60e6,        # C3, one launch
     "prepass": 40.87e6 + 0.46e6,     # C4 QKV pre-pass (MOD), one launch; the 20.4 MB int8 output stays in L2
     "decode": 15.78e6 * 19456 / 6144,  # captured on the 6144-row qkv GEMV; bytes grow with rows (2568 B per row)
-    "dit": 115.8e6 + 78.2e6,         # mean over the 32 W8A8 GEMM launches of one DiT step
+    "dit": 113.8e6 + 52.1e6,         # mean over the 32 W8A8 GEMM launches of one DiT step
 }
 
 
