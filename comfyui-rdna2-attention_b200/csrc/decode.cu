@@ -73,16 +73,32 @@ constexpr int GEMV_UNROLL = 4;   // 512-value steps in flight per row
 
 // x is staged in shared memory in reading order: step s, sub-chunk j, lane l -> float4 index (s*4+j)*32+l,
 // so each float4 read of a warp is conflict-free. K % 16 == 0; a partial last step is masked.
+// silu(g) u in fp32 as torch computes silu(gate) * up: g / (1 + exp(-g)), then the product.
+__device__ __forceinline__ float silu_mul_f32(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+}
+
+// act 1: x holds [gate | up] (2K values) and the GEMV input is silu(gate) * up, formed while x is staged.
+// residual: out[n] = residual[n] + y[n].
 __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_i8_kernel(const float* __restrict__ x, const int8_t* __restrict__ w,
                                                                  const float* __restrict__ scale,
-                                                                 const float* __restrict__ bias, float* __restrict__ out,
-                                                                 int N, int K) {
+                                                                 const float* __restrict__ bias,
+                                                                 const float* __restrict__ residual, float* __restrict__ out,
+                                                                 int N, int K, int act) {
     extern __shared__ float4 xs[];
     const int steps = (K + 511) / 512;
     for (int i = threadIdx.x; i < steps * 128; i += blockDim.x) {
         const int s = i >> 7, r = i & 127, l = r >> 2, j = r & 3;
         const int k = i * 4;
-        xs[(s * 4 + j) * 32 + l] = k < K ? *reinterpret_cast<const float4*>(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < K) {
+            v = *reinterpret_cast<const float4*>(x + k);
+            if (act) {
+                const float4 u = *reinterpret_cast<const float4*>(x + K + k);
+                v = make_float4(silu_mul_f32(v.x, u.x), silu_mul_f32(v.y, u.y), silu_mul_f32(v.z, u.z), silu_mul_f32(v.w, u.w));
+            }
+        }
+        xs[(s * 4 + j) * 32 + l] = v;
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -124,10 +140,70 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_i8_kernel(const float* _
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         const int n = row0 + r;
         if (lane == 0 && n < N) {
-            const float y = v * scale[n];
-            out[n] = bias ? y + bias[n] : y;
+            float y = v * scale[n];
+            if (bias) y += bias[n];
+            out[n] = residual ? __fadd_rn(residual[n], y) : y;
         }
     }
+}
+
+// ---------------------------------------------------------------- decode step glue
+// y = x * rsqrt(mean(x^2) + eps) * w for one fp32 row (torch's rms(x, w) of the decode step), one CTA.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();  // red may still be read from a previous call
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
+
+__global__ void __launch_bounds__(1024) rms_norm_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                           float* __restrict__ y, int D, float eps) {
+    __shared__ float red[32];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    ss = block_sum(ss, red);
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+    for (int i = threadIdx.x; i < D; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], r), w[i]);
+}
+
+// After the q|k|v GEMV of one token: per head of 128, q and k get RMSNorm (q_norm / k_norm weights) and the
+// half-split rotary embedding at position *pos (angle pos * inv_freq[i], pairs (i, i + 64)); q goes to q_out, k and
+// v into the caches' row *pos ([capacity][kv_heads][128] each). One CTA of 128 threads per head (q heads, then k,
+// then v).
+__global__ void __launch_bounds__(HEAD) decode_qk_rope_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
+                                                             const float* __restrict__ k_norm,
+                                                             const float* __restrict__ inv_freq,
+                                                             const int64_t* __restrict__ pos, float* __restrict__ q_out,
+                                                             float* __restrict__ k_cache, float* __restrict__ v_cache,
+                                                             int heads, int kv_heads, float eps) {
+    __shared__ float red[4];
+    __shared__ float ys[HEAD];
+    const int hd = blockIdx.x, t = threadIdx.x;
+    const int64_t p = *pos;
+    const float x = qkv[(int64_t)hd * HEAD + t];
+    if (hd >= heads + kv_heads) {  // v: copied into the cache
+        v_cache[(p * kv_heads + (hd - heads - kv_heads)) * HEAD + t] = x;
+        return;
+    }
+    const bool is_q = hd < heads;
+    const float ss = block_sum(__fmul_rn(x, x), red);
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)HEAD), eps));
+    ys[t] = __fmul_rn(__fmul_rn(x, r), (is_q ? q_norm : k_norm)[t]);
+    __syncthreads();
+    const int i = t & 63;
+    const float ang = __fmul_rn((float)p, inv_freq[i]);
+    const float c = cosf(ang), sn = sinf(ang);
+    const float a = ys[i], b = ys[i + 64];
+    const float o = t < 64 ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+    if (is_q)
+        q_out[(int64_t)hd * HEAD + t] = o;
+    else
+        k_cache[(p * kv_heads + (hd - heads)) * HEAD + t] = o;
 }
 
 // ---------------------------------------------------------------- decode attention
@@ -252,9 +328,44 @@ extern "C" int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, c
     if (smem > 48 * 1024)
         if (int rc = set_smem(gemv_i8_kernel, smem)) return rc;
     const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
-    gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(x, w, scale, bias,
-                                                                                                       out, N, K);
+    gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(
+        x, w, scale, bias, nullptr, out, N, K, 0);
     return check_launch("gemv_i8_kernel");
+}
+
+extern "C" int b2_gemv_i8_ex(const float* x, const int8_t* w, const float* scale, const float* bias, const float* residual,
+                             float* out, int N, int K, int act, void* stream) {
+    if (!x || !w || !scale || !out || N < 0 || K <= 0) return fail(B2_ERR_INVALID, "gemv_i8_ex: bad arguments");
+    if (act != 0 && act != 1) return fail(B2_ERR_INVALID, "gemv_i8_ex: act %d (0: none, 1: silu(gate) * up)", act);
+    if (K % 16) return fail(B2_ERR_UNSUPPORTED, "gemv_i8_ex: K=%d must be a multiple of 16", K);
+    if (!aligned16(x) || !aligned16(w)) return fail(B2_ERR_UNSUPPORTED, "gemv_i8_ex: x and w must be 16-byte aligned");
+    if (residual == out) return fail(B2_ERR_INVALID, "gemv_i8_ex: residual and out must not alias");
+    if (N == 0) return B2_OK;
+    const int steps = (K + 511) / 512;
+    const int smem = steps * 512 * 4;
+    if (smem > 200 * 1024) return fail(B2_ERR_UNSUPPORTED, "gemv_i8_ex: K=%d too large", K);
+    if (smem > 48 * 1024)
+        if (int rc = set_smem(gemv_i8_kernel, smem)) return rc;
+    const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
+    gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(
+        x, w, scale, bias, residual, out, N, K, act);
+    return check_launch("gemv_i8_kernel");
+}
+
+extern "C" int b2_rms_norm_f32(const float* x, const float* w, float* y, int D, float eps, void* stream) {
+    if (!x || !w || !y || D <= 0) return fail(B2_ERR_INVALID, "rms_norm_f32: bad arguments");
+    rms_norm_f32_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, w, y, D, eps);
+    return check_launch("rms_norm_f32_kernel");
+}
+
+extern "C" int b2_decode_qk_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* inv_freq,
+                                 const int64_t* pos, float* q_out, float* k_cache, float* v_cache, int heads,
+                                 int kv_heads, float eps, void* stream) {
+    if (!qkv || !q_norm || !k_norm || !inv_freq || !pos || !q_out || !k_cache || !v_cache || heads <= 0 || kv_heads <= 0)
+        return fail(B2_ERR_INVALID, "decode_qk_rope: bad arguments");
+    decode_qk_rope_kernel<<<heads + 2 * kv_heads, HEAD, 0, (cudaStream_t)stream>>>(qkv, q_norm, k_norm, inv_freq, pos, q_out,
+                                                                                   k_cache, v_cache, heads, kv_heads, eps);
+    return check_launch("decode_qk_rope_kernel");
 }
 
 extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out,

@@ -2,12 +2,14 @@
 
 Architecture (the configuration's): hidden 2560, 36 layers, 32 query / 8 KV heads of 128, SwiGLU MLP 9728, RMSNorm,
 per-output-channel int8 linears read by the HBM-streaming GEMV, fp32 activations and fp32 decode attention over a
-fixed-capacity KV cache (int8_gemv.py:117-126). Per layer the step is
+fixed-capacity KV cache (int8_gemv.py:117-126). Per layer the step is 9 launches:
   RMSNorm -> GEMV(q|k|v) -> QK-norm + rope + KV-cache write -> decode attention (split 32 + merge)
-  -> GEMV(o) + residual -> RMSNorm -> GEMV(gate|up) -> SiLU * up -> GEMV(down) + residual.
-The q/k/v and gate/up weights of a layer are stored concatenated, so each is one GEMV over one x. The small
-element-wise ops are torch ops; the whole step is captured once in a CUDA graph and replayed (the position and the
-cache length live on the device, as in the reference, int8_gemv.hip:121-131).
+  -> GEMV(o) with the residual in its epilogue -> RMSNorm -> GEMV(gate|up) -> GEMV(down) reading silu(gate) * up
+  as its input and adding the residual.
+The q/k/v and gate/up weights of a layer are stored concatenated, so each is one GEMV over one x. The whole step is
+captured once in a CUDA graph and replayed (the position and the cache length live on the device, as in the
+reference, int8_gemv.hip:121-131). `layer_reference` is the same layer with the element-wise work as torch ops
+(about 25 launches per layer), kept as the reference the fused layer is tested against.
 """
 import dataclasses
 
@@ -74,6 +76,14 @@ class TextDecoder:
         self.partial = torch.empty((H, ops.DECODE_SPLITS, d), dtype=torch.float32, device=device)
         self.stats = torch.empty((H, ops.DECODE_SPLITS, 2), dtype=torch.float32, device=device)
         self.att = torch.empty((1, 1, H, d), dtype=torch.float32, device=device)
+        D, F = cfg.hidden, cfg.mlp
+        self.h = torch.empty((D,), dtype=torch.float32, device=device)
+        self.x2 = torch.empty((D,), dtype=torch.float32, device=device)
+        self.xb = torch.empty((D,), dtype=torch.float32, device=device)
+        self.qkv = torch.empty(((H + 2 * Hk) * d,), dtype=torch.float32, device=device)
+        self.q = torch.empty((H, d), dtype=torch.float32, device=device)
+        self.gu = torch.empty((2 * F,), dtype=torch.float32, device=device)
+        self.fused = True
         self.graph = None
 
     def rope(self, t):
@@ -83,7 +93,22 @@ class TextDecoder:
         a, b = t[:, :64], t[:, 64:]
         return torch.cat((a * cos - b * sin, a * sin + b * cos), dim=-1)
 
-    def layer(self, L, x):
+    def layer(self, L, x, out):
+        """x [D] -> out [D] (distinct buffers) through the fused kernels."""
+        cfg = self.cfg
+        H, Hk, d = cfg.heads, cfg.kv_heads, cfg.head_dim
+        ops.rms_norm_f32(x, L.norm_in, cfg.eps, out=self.h)
+        ops.gemv_i8(self.h, L.w_qkv, L.s_qkv, out=self.qkv)
+        ops.decode_qk_rope(self.qkv, L.q_norm, L.k_norm, self.inv_freq, self.pos, self.q, L.k_cache, L.v_cache, H, Hk,
+                           cfg.eps)
+        ops.attn_decode(self.q.view(1, 1, H, d), L.k_cache, L.v_cache, self.lengths, d ** -0.5, out=self.att,
+                        partial=self.partial, stats=self.stats)
+        ops.gemv_i8_ex(self.att.reshape(-1), L.w_o, L.s_o, residual=x, out=self.x2)
+        ops.rms_norm_f32(self.x2, L.norm_post, cfg.eps, out=self.h)
+        ops.gemv_i8(self.h, L.w_gu, L.s_gu, out=self.gu)
+        return ops.gemv_i8_ex(self.gu, L.w_down, L.s_down, residual=self.x2, silu_mul=True, out=out)
+
+    def layer_reference(self, L, x):
         cfg = self.cfg
         H, Hk, d, F = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.mlp
         h = rms(x, L.norm_in, cfg.eps)
@@ -103,10 +128,17 @@ class TextDecoder:
         return x + ops.gemv_i8(a, L.w_down, L.s_down).view(1, -1)
 
     def step_eager(self):
-        x = self.x
-        for L in self.layers:
-            x = self.layer(L, x)
-        self.x.copy_(x)
+        if not self.fused:
+            x = self.x
+            for L in self.layers:
+                x = self.layer_reference(L, x)
+            self.x.copy_(x)
+            return self.x
+        bufs = (self.x.view(-1), self.xb)
+        for i, L in enumerate(self.layers):
+            self.layer(L, bufs[i & 1], bufs[(i + 1) & 1])
+        if len(self.layers) & 1:
+            self.x.view(-1).copy_(self.xb)
         return self.x
 
     def capture(self):
@@ -141,4 +173,4 @@ class TextDecoder:
         kv = cfg.layers * 2 * cfg.capacity * cfg.kv_heads * cfg.head_dim * 4
         return w + s + kv, w
 
-    launches_per_layer = 6  # 4 GEMVs + decode attention (2 kernels)
+    launches_per_layer = 9  # 2 RMSNorms, 4 GEMVs, q/k rope, decode attention (2 kernels)

@@ -228,6 +228,37 @@ def gemv_i8(x, w, scale, bias=None, out=None):
     return out
 
 
+def gemv_i8_ex(x, w, scale, bias=None, residual=None, silu_mul=False, out=None):
+    """gemv_i8 for the decode step: with silu_mul, x = [gate | up] (2K values) and the input is silu(gate) * up;
+    with a residual, the result is residual + y."""
+    require_cuda(x, w, scale, bias, residual)
+    N, K = w.shape
+    if x.dtype != torch.float32 or x.numel() != (2 * K if silu_mul else K) or not x.is_contiguous():
+        raise RuntimeError("gemv_i8_ex needs one contiguous fp32 row of K (2K with silu_mul) values")
+    out = torch.empty((N,), dtype=torch.float32, device=x.device) if out is None else out
+    call("b2_gemv_i8_ex", ptr(x), ptr(w), ptr(scale), ptr(bias), ptr(residual), ptr(out), I(N), I(K), I(1 if silu_mul else 0),
+         stream())
+    return out
+
+
+def rms_norm_f32(x, w, eps, out=None):
+    """One fp32 row: x * rsqrt(mean(x^2) + eps) * w."""
+    require_cuda(x, w)
+    out = torch.empty_like(x) if out is None else out
+    call("b2_rms_norm_f32", ptr(x), ptr(w), ptr(out), I(x.numel()), F(eps), stream())
+    return out
+
+
+def decode_qk_rope(qkv, q_norm, k_norm, inv_freq, pos, q_out, k_cache, v_cache, heads, kv_heads, eps):
+    """q/k RMSNorm + rotary at device position pos (int64 [1]) for one token; k and v into the caches' row pos."""
+    require_cuda(qkv, q_norm, k_norm, inv_freq, pos, q_out, k_cache, v_cache)
+    if pos.dtype != torch.int64 or not all(t.is_contiguous() for t in (qkv, q_out, k_cache, v_cache)):
+        raise RuntimeError("decode_qk_rope needs contiguous fp32 buffers and an int64 position")
+    call("b2_decode_qk_rope", ptr(qkv), ptr(q_norm), ptr(k_norm), ptr(inv_freq), ptr(pos), ptr(q_out), ptr(k_cache),
+         ptr(v_cache), I(heads), I(kv_heads), F(eps), stream())
+    return q_out
+
+
 DECODE_SPLITS = 32
 
 

@@ -148,6 +148,20 @@ int b2_rotate(const float* x, float* out, int64_t n, int group, void* stream);
  * int8_gemv.py:62-63). K % 16 == 0. */
 int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
                void* stream);
+/* Decode-step glue of the configuration-5 driver (no counterpart entry points in the reference, whose decode step
+ * runs these as torch ops around int8_gemv.py's kernels):
+ *   b2_gemv_i8_ex: b2_gemv_i8 with act = 1 taking x = [gate | up] (2K values) and using silu(gate) * up as the input
+ *     (torch's silu(g) * u in fp32), and an optional residual: out[n] = residual[n] + y[n] (residual != out).
+ *   b2_rms_norm_f32: y = x * rsqrt(mean(x^2) + eps) * w for one fp32 row of D values.
+ *   b2_decode_qk_rope: after the q|k|v GEMV, per head of 128: RMSNorm of q (q_norm) and k (k_norm), half-split
+ *     rotary embedding at position *pos (angles *pos * inv_freq[0..63]), q to q_out [heads][128], k and v into row
+ *     *pos of the caches [capacity][kv_heads][128]. */
+int b2_gemv_i8_ex(const float* x, const int8_t* w, const float* scale, const float* bias, const float* residual,
+                  float* out, int N, int K, int act, void* stream);
+int b2_rms_norm_f32(const float* x, const float* w, float* y, int D, float eps, void* stream);
+int b2_decode_qk_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* inv_freq,
+                      const int64_t* pos, float* q_out, float* k_cache, float* v_cache, int heads, int kv_heads,
+                      float eps, void* stream);
 /* fp32 split-KV decode attention + merge (int8_gemv.hip:198-271 attn_decode/attn_merge;
  * int8_gemv.py:101-114). q [B,1,H,128], k/v [B,capacity,Hkv,128], lengths int32 [B] read on the
  * device (graph-replayable), out [B,1,H,128]. partial: fp32 [B*H, 32, 128], stats: fp32 [B*H, 32, 2]

@@ -117,3 +117,26 @@ def test_attn_decode(pkg, dev, B, H, Hkv, cap, lengths):
     got = pkg.int8_gemv.attention_decode(dev_(q, dev), dev_(k, dev), dev_(v, dev), dev_(ln, dev)).cpu().numpy()
     ref = odec.attn_decode(q, k, v, ln, 128 ** -0.5)
     assert oatt.rel_l2(got, ref) < 1e-5
+
+
+def test_decoder_fused_step_matches_torch_ops(pkg, dev):
+    """The configuration-5 decode step on the fused kernels (9 launches per layer) against the same layer written
+    with torch element-wise ops: two consecutive tokens, hidden state and KV caches."""
+    import importlib
+
+    decoder = importlib.import_module(pkg.__name__ + ".decoder")
+    cfg = decoder.DecoderConfig(hidden=512, layers=3, heads=8, kv_heads=2, head_dim=128, mlp=1024, capacity=64)
+    fused, ref = decoder.TextDecoder(cfg, dev, seed=1), decoder.TextDecoder(cfg, dev, seed=1)
+    ref.fused = False
+    x0 = torch.randn((1, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(5), device=dev)
+    for dec in (fused, ref):
+        dec.x.copy_(x0)
+    for pos in (37, 38):
+        for dec in (fused, ref):
+            dec.set_position(pos)
+            dec.step_eager()
+        rel = ((fused.x - ref.x).norm() / ref.x.norm()).item()
+        assert rel < 2e-5, (pos, rel)
+    for lf, lr in zip(fused.layers, ref.layers):
+        assert torch.allclose(lf.k_cache, lr.k_cache, rtol=1e-5, atol=1e-6)
+        assert torch.equal(lf.v_cache, lr.v_cache) or torch.allclose(lf.v_cache, lr.v_cache, rtol=1e-5, atol=1e-6)
