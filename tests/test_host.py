@@ -57,6 +57,12 @@ def test_validation_errors_before_any_launch(pkg):
                    I64(128), fake, I64(0), I64(0), I64(128), I(1), I(3), I(2), I(4), I(4), F(1.0), I(0), P(None), I64(0), P(None)) == 1
     # rms_norm: D bound
     assert _status(pkg, "b2_rms_norm", fake, fake, fake, I(1), I(8200), I(1), I(1), I64(0), I64(0), I64(8200), F(1e-6), P(None)) == 2
+    # SwiGLU GEMM: 2F must be a multiple of 256; GEMV with silu: act in {0, 1}, residual must not alias out
+    assert _status(pkg, "b2_gemm_swiglu", fake, fake, fake, fake, fake, I(8), I(384), I(16), P(None)) == 2
+    assert _status(pkg, "b2_gemv_i8_ex", fake, fake, fake, P(None), P(None), fake, I(8), I(16), I(2), P(None)) == 1
+    assert _status(pkg, "b2_gemv_i8_ex", fake, fake, fake, P(None), fake, fake, I(8), I(16), I(0), P(None)) == 1
+    assert _status(pkg, "b2_decode_qk_rope", fake, fake, fake, fake, P(None), fake, fake, fake, I(8), I(2), F(1e-6),
+                   P(None)) == 1
     # empty problems succeed without launching
     assert _status(pkg, "b2_gemm_i32", fake, fake, fake, I(0), I(8), I(16), P(None)) == 0
     assert _status(pkg, "b2_quant_pack_a", fake, I64(16), fake, fake, I(0), I(16), I(0), P(None)) == 0
@@ -137,3 +143,16 @@ def test_enable_installs_and_removes_patches(pkg):
         g.originals.clear()
         g.pending = None
         g.fusable = False
+
+
+def test_swiglu_interleave_pairs_gate_and_up_blocks(pkg):
+    """Row i of the interleaved gate/up weight: block j = i // 256 holds gate rows [128 j, 128 j + 128) then the
+    matching up rows [F + 128 j, F + 128 j + 128)."""
+    F = 640
+    idx = pkg.ops.swiglu_interleave(2 * F).tolist()
+    assert sorted(idx) == list(range(2 * F))
+    for i, r in enumerate(idx):
+        j, o = divmod(i, 256)
+        assert r == (128 * j + o if o < 128 else F + 128 * j + o - 128)
+    with pytest.raises(RuntimeError):
+        pkg.ops.swiglu_interleave(2 * 600)
