@@ -686,6 +686,8 @@ class DiTC4:
         self.config = {"workload": "C4 DiT block stack", "blocks": 8, "batch": 2, "tokens": 3321, "hidden": 3072,
                        "heads": 24, "mlp": 8192, "weights": "W8A8 per-channel int8, block-128 Hadamard",
                        "l2": "weights 0.9 GB per step, inputs larger than L2",
+                       "e2e": "per step: pinned host input -> device and result -> pinned host on a copy stream, the next "
+                              "step's input and the previous step's result overlapping this step's compute",
                        "shard": {"branches": [plan.batch_lo, plan.batch_hi], "heads": [plan.head_lo, plan.head_hi],
                                  "group": list(plan.group_ranks)}}
 
