@@ -39,6 +39,7 @@ SIGNATURES = {
     "b2_rotate": (I, [P, P, I64, I, P]),
     "b2_gemv_i8": (I, [P, P, P, P, P, I, I, P]),
     "b2_gemv_i8_ex": (I, [P, P, P, P, P, P, I, I, I, P]),
+    "b2_gemv_bf16": (I, [P, P, P, I, I, P]),
     "b2_rms_norm_f32": (I, [P, P, P, I, F, P]),
     "b2_decode_qk_rope": (I, [P, P, P, P, P, P, P, P, I, I, F, P]),
     "b2_attn_decode": (I, [P, P, P, P, P, P, P, I, I, I, I, F, P]),

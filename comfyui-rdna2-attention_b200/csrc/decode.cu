@@ -147,6 +147,74 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_i8_kernel(const float* _
     }
 }
 
+// ---------------------------------------------------------------- gemv_bf16
+// out[n] = sum_k w[n,k] x[k] for a bf16 table (the LM head of a decoder with tied embeddings). Same streaming
+// scheme as gemv_i8: 16-byte non-allocating loads (8 bf16), GEMV_UNROLL steps of 256 values in flight for each of a
+// warp's GEMV_ROWS rows. bf16 -> fp32 is exact: the high half of a word already is the fp32 pattern, the low half
+// shifted up by 16 is.
+__device__ __forceinline__ float dot8_bf16(const uint4 w, const float4 (&x)[2], float acc) {
+    acc = fmaf(__uint_as_float(w.x << 16), x[0].x, acc);
+    acc = fmaf(__uint_as_float(w.x & 0xffff0000u), x[0].y, acc);
+    acc = fmaf(__uint_as_float(w.y << 16), x[0].z, acc);
+    acc = fmaf(__uint_as_float(w.y & 0xffff0000u), x[0].w, acc);
+    acc = fmaf(__uint_as_float(w.z << 16), x[1].x, acc);
+    acc = fmaf(__uint_as_float(w.z & 0xffff0000u), x[1].y, acc);
+    acc = fmaf(__uint_as_float(w.w << 16), x[1].z, acc);
+    acc = fmaf(__uint_as_float(w.w & 0xffff0000u), x[1].w, acc);
+    return acc;
+}
+
+// x staged in reading order: step s (256 values), half j, lane l -> float4 index (s*2+j)*32+l holds
+// x[s*256 + l*8 + 4j .. +3]. K % 8 == 0; a partial last step is masked per lane.
+__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_bf16_kernel(const float* __restrict__ x,
+                                                                   const uint16_t* __restrict__ w,
+                                                                   float* __restrict__ out, int N, int K) {
+    extern __shared__ float4 xs[];
+    const int steps = (K + 255) / 256;
+    for (int i = threadIdx.x; i < steps * 64; i += blockDim.x) {
+        const int s = i >> 6, r = i & 63, l = r >> 1, j = r & 1;
+        const int k = i * 4;
+        xs[(s * 2 + j) * 32 + l] = k < K ? *reinterpret_cast<const float4*>(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS;
+    if (row0 >= N) return;
+    float acc[GEMV_ROWS] = {};
+    const uint16_t* wr[GEMV_ROWS];
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r) wr[r] = w + (int64_t)min(row0 + r, N - 1) * K + lane * 8;
+    const bool full_steps = (K % 256) == 0;
+    int s = 0;
+    for (; s + GEMV_UNROLL <= steps && (full_steps || s + GEMV_UNROLL < steps); s += GEMV_UNROLL) {
+        uint4 v[GEMV_UNROLL][GEMV_ROWS];
+#pragma unroll
+        for (int u = 0; u < GEMV_UNROLL; ++u)
+#pragma unroll
+            for (int r = 0; r < GEMV_ROWS; ++r) v[u][r] = ld_stream(wr[r] + (s + u) * 256);
+#pragma unroll
+        for (int u = 0; u < GEMV_UNROLL; ++u) {
+            const float4 xv[2] = {xs[((s + u) * 2) * 32 + lane], xs[((s + u) * 2 + 1) * 32 + lane]};
+#pragma unroll
+            for (int r = 0; r < GEMV_ROWS; ++r) acc[r] = dot8_bf16(v[u][r], xv, acc[r]);
+        }
+    }
+    for (; s < steps; ++s) {
+        if (s * 256 + lane * 8 >= K) break;
+        const float4 xv[2] = {xs[(s * 2) * 32 + lane], xs[(s * 2 + 1) * 32 + lane]};
+#pragma unroll
+        for (int r = 0; r < GEMV_ROWS; ++r) acc[r] = dot8_bf16(ld_stream(wr[r] + s * 256), xv, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r) {
+        float v = acc[r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const int n = row0 + r;
+        if (lane == 0 && n < N) out[n] = v;
+    }
+}
+
 // ---------------------------------------------------------------- decode step glue
 // y = x * rsqrt(mean(x^2) + eps) * w for one fp32 row (torch's rms(x, w) of the decode step), one CTA.
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -350,6 +418,22 @@ extern "C" int b2_gemv_i8_ex(const float* x, const int8_t* w, const float* scale
     gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(
         x, w, scale, bias, residual, out, N, K, act);
     return check_launch("gemv_i8_kernel");
+}
+
+extern "C" int b2_gemv_bf16(const float* x, const uint16_t* w, float* out, int N, int K, void* stream) {
+    if (!x || !w || !out || N < 0 || K <= 0) return fail(B2_ERR_INVALID, "gemv_bf16: bad arguments");
+    if (K % 8) return fail(B2_ERR_UNSUPPORTED, "gemv_bf16: K=%d must be a multiple of 8", K);
+    if (!aligned16(x) || !aligned16(w)) return fail(B2_ERR_UNSUPPORTED, "gemv_bf16: x and w must be 16-byte aligned");
+    if (N == 0) return B2_OK;
+    const int steps = (K + 255) / 256;
+    const int smem = steps * 256 * 4;
+    if (smem > 200 * 1024) return fail(B2_ERR_UNSUPPORTED, "gemv_bf16: K=%d too large", K);
+    if (smem > 48 * 1024)
+        if (int rc = set_smem(gemv_bf16_kernel, smem)) return rc;
+    const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
+    gemv_bf16_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(x, w, out, N,
+                                                                                                            K);
+    return check_launch("gemv_bf16_kernel");
 }
 
 extern "C" int b2_rms_norm_f32(const float* x, const float* w, float* y, int D, float eps, void* stream) {

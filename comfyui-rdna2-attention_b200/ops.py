@@ -241,6 +241,19 @@ def gemv_i8_ex(x, w, scale, bias=None, residual=None, silu_mul=False, out=None):
     return out
 
 
+def gemv_bf16(x, w, out=None):
+    """fp32 [N] = w bf16 [N, K] . x fp32 [K] (the logits of a tied-embedding decoder)."""
+    require_cuda(x, w)
+    if w.dtype != torch.bfloat16 or w.dim() != 2 or not w.is_contiguous():
+        raise RuntimeError("gemv_bf16 needs a contiguous bf16 [N, K] table")
+    N, K = w.shape
+    if x.dtype != torch.float32 or x.numel() != K or not x.is_contiguous():
+        raise RuntimeError("gemv_bf16 needs one contiguous fp32 row of K values")
+    out = torch.empty((N,), dtype=torch.float32, device=x.device) if out is None else out
+    call("b2_gemv_bf16", ptr(x), ptr(w), ptr(out), I(N), I(K), stream())
+    return out
+
+
 def rms_norm_f32(x, w, eps, out=None):
     """One fp32 row: x * rsqrt(mean(x^2) + eps) * w."""
     require_cuda(x, w)

@@ -148,6 +148,9 @@ int b2_rotate(const float* x, float* out, int64_t n, int group, void* stream);
  * int8_gemv.py:62-63). K % 16 == 0. */
 int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
                void* stream);
+/* out[n] = sum_k w[n,k] x[k] in fp32 for a bf16 table w [N, K] (int8_gemv.hip:87-119 gemv_bf16; the logits of
+ * int8_gemv.py:87-98). K % 8 == 0 (the reference: K % 256, N % 16); x and w 16-byte aligned. */
+int b2_gemv_bf16(const float* x, const uint16_t* w, float* out, int N, int K, void* stream);
 /* Decode-step glue of the configuration-5 driver (no counterpart entry points in the reference, whose decode step
  * runs these as torch ops around int8_gemv.py's kernels):
  *   b2_gemv_i8_ex: b2_gemv_i8 with act = 1 taking x = [gate | up] (2K values) and using silu(gate) * up as the input

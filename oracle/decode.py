@@ -32,6 +32,18 @@ def gemv_i8(x, w, scale, bias=None):
     return y.astype(F32)
 
 
+def bf16_to_f32(bits):
+    """bf16 bit patterns (uint16) -> float32, exactly: the pattern is the high half of the float32."""
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << np.uint32(16)).view(F32)
+
+
+def gemv_bf16(x, w_bits):
+    """out[n] = sum_k w[n, k] x[k] for a bf16 table (int8_gemv.hip:87-119 gemv_bf16, the logits of
+    int8_gemv.py:87-98), the table given as uint16 bit patterns, accumulated in float64 here."""
+    w = bf16_to_f32(w_bits).astype(np.float64)
+    return (w @ np.asarray(x, np.float64).reshape(-1)).astype(F32)
+
+
 def linear_fallback(x, w, scale, bias=None):
     """The reference's non-GEMV path in fp32 torch semantics: F.linear(x, w.to(fp32) * scale, bias)
     (int8_gemv.py:58-59), used as the CPU baseline."""

@@ -63,6 +63,10 @@ def test_validation_errors_before_any_launch(pkg):
     assert _status(pkg, "b2_gemv_i8_ex", fake, fake, fake, P(None), fake, fake, I(8), I(16), I(0), P(None)) == 1
     assert _status(pkg, "b2_decode_qk_rope", fake, fake, fake, fake, P(None), fake, fake, fake, I(8), I(2), F(1e-6),
                    P(None)) == 1
+    # bf16 GEMV: K % 8, null table
+    assert _status(pkg, "b2_gemv_bf16", fake, fake, fake, I(16), I(12), P(None)) == 2
+    assert _status(pkg, "b2_gemv_bf16", fake, P(None), fake, I(16), I(16), P(None)) == 1
+    assert _status(pkg, "b2_gemv_bf16", fake, fake, fake, I(0), I(16), P(None)) == 0
     # empty problems succeed without launching
     assert _status(pkg, "b2_gemm_i32", fake, fake, fake, I(0), I(8), I(16), P(None)) == 0
     assert _status(pkg, "b2_quant_pack_a", fake, I64(16), fake, fake, I(0), I(16), I(0), P(None)) == 0
@@ -156,3 +160,62 @@ def test_swiglu_interleave_pairs_gate_and_up_blocks(pkg):
         assert r == (128 * j + o if o < 128 else F + 128 * j + o - 128)
     with pytest.raises(RuntimeError):
         pkg.ops.swiglu_interleave(2 * 600)
+
+
+def test_decode_routing_follows_the_reference(pkg):
+    """int8_gemv keeps the reference's routing (int8_gemv.py:49-50,68-69,88-89): prompt encoding, batches and
+    non-fp32 inputs go to the module's own forward and never reach the library; patch() installs the linear, MLP,
+    logits, generate and KV-cache patches on duck-typed modules."""
+    gv = pkg.int8_gemv
+
+    class Linear:
+        quant_format = "int8_tensorwise"
+        weight_function, bias_function = [], []
+
+        def forward(self, x):
+            return "core linear"
+
+    class MLP:
+        merged_mlp = False
+
+        def forward(self, x, norm=None):
+            return "core mlp"
+
+    class BaseQwen3:
+        def logits(self, x):
+            return "core logits"
+
+    class Qwen3_4B(BaseQwen3):
+        pass
+
+    lin = Linear()
+    assert gv.linear_forward(lin, 8, 16, torch.int8, 0, torch.zeros((1, 3, 16))) == "core linear"
+    assert gv.linear_forward(lin, 8, 16, torch.int8, 1024, torch.zeros((1, 3, 16))) == "core linear"
+    assert gv.linear_forward(lin, 8, 16, torch.int8, 0, torch.zeros((1, 1, 16), dtype=torch.float16)) == "core linear"
+    mlp = MLP()
+    mlp.gate_proj, mlp.up_proj = Linear(), Linear()
+    assert gv.mlp_forward(mlp, torch.int8, torch.zeros((1, 3, 16))) == "core mlp"
+    gv.generating = True
+    try:
+        assert gv.mlp_forward(mlp, torch.int8, torch.zeros((1, 1, 16))) == "core mlp"
+    finally:
+        gv.generating = False
+    qwen = Qwen3_4B()
+    embed = types.SimpleNamespace(weight=torch.zeros((32, 16), dtype=torch.bfloat16), weight_function=[], bias_function=[])
+    config = types.SimpleNamespace(lm_head=False, head_dim=128, num_attention_heads=32, num_key_value_heads=8)
+    qwen.model = types.SimpleNamespace(embed_tokens=embed, config=config, fixed_kv=True)
+    assert gv.logits(qwen, torch.zeros((2, 3, 16))) == "core logits"
+
+    lin.weight = types.SimpleNamespace(shape=(8, 16), dtype=torch.int8,
+                                       _params=types.SimpleNamespace(scale=torch.ones(8), transposed=False,
+                                                                     convrot=False, convrot_groupsize=0))
+    mlp.gate_proj.weight = types.SimpleNamespace(dtype=torch.int8)
+    patches = {}
+    modules = [("layers.0.lin", lin), ("layers.0.mlp", mlp), ("", qwen)]
+    clip = types.SimpleNamespace(patcher=types.SimpleNamespace(
+        model=types.SimpleNamespace(named_modules=lambda: modules),
+        add_object_patch=lambda name, fn: patches.__setitem__(name, fn)))
+    gv.patch(clip)
+    assert sorted(patches) == [".generate", ".logits", ".model.init_kv_cache", "layers.0.lin.forward", "layers.0.mlp.forward"]
+    assert patches["layers.0.mlp.forward"].func is gv.mlp_forward
+    assert patches[".logits"].func is gv.logits

@@ -3,6 +3,8 @@
 RMSNorm: within two fp16 steps of the oracle (the fp32 sum order and rsqrt differ from the reference's), with at
 most 2e-3 of the values off. Decode: rotate bit-exact; GEMV and decode attention within 1e-5 relative L2 of float64.
 """
+import types
+
 import numpy as np
 import pytest
 import torch
@@ -88,6 +90,69 @@ def test_gemv_i8(pkg, dev, N, K):
         got = pkg.ops.gemv_i8(dev_(x, dev), dev_(w, dev), dev_(s, dev), None if bias is None else dev_(bias, dev))
         ref = odec.gemv_i8(x, w, s, bias)
         assert oatt.rel_l2(got.cpu().numpy(), ref) < 1e-5
+
+
+@pytest.mark.parametrize("N,K", [(151936, 2560), (4096, 2560), (16, 256), (37, 264), (5, 8), (1000, 1288)])
+def test_gemv_bf16(pkg, dev, N, K):
+    """The logits GEMV on a bf16 table, including ragged K (a partial last 256-value step) and N off the 16-row CTA."""
+    g = np.random.default_rng(N * 7 + K)
+    x = g.standard_normal(K).astype(F32)
+    wt = torch.from_numpy((g.standard_normal((N, K)) * 0.05).astype(F32)).to(torch.bfloat16)
+    got = pkg.ops.gemv_bf16(dev_(x, dev), wt.to(dev)).cpu().numpy()
+    ref = odec.gemv_bf16(x, wt.view(torch.int16).numpy().view(np.uint16))
+    assert oatt.rel_l2(got, ref) < 1e-5
+
+
+def test_logits_drop_in(pkg, dev):
+    """int8_gemv.logits: the last position of one fp32 sequence against the tied bf16 table, shape (1, 1, vocab)."""
+    N, K = 4096, 2560
+    g = np.random.default_rng(5)
+    table = torch.from_numpy((g.standard_normal((N, K)) * 0.05).astype(F32)).to(torch.bfloat16)
+    x = g.standard_normal((1, 7, K)).astype(F32)
+    embed = types.SimpleNamespace(weight=table.to(dev), weight_function=[], bias_function=[])
+    transformer = types.SimpleNamespace(model=types.SimpleNamespace(embed_tokens=embed))
+    got = pkg.int8_gemv.logits(transformer, dev_(x, dev))
+    assert got.shape == (1, 1, N) and got.dtype == torch.float32
+    ref = odec.gemv_bf16(x[0, -1], table.view(torch.int16).numpy().view(np.uint16))
+    assert oatt.rel_l2(got.cpu().numpy().reshape(-1), ref) < 1e-5
+
+
+def _int8_linear(w, s, dev):
+    weight = types.SimpleNamespace(_qdata=dev_(w, dev), _params=types.SimpleNamespace(scale=dev_(s, dev)))
+    return types.SimpleNamespace(weight=weight, bias=None, weight_function=[], bias_function=[])
+
+
+def test_prefill_paths_while_generating(pkg, dev):
+    """While generating: a multi-token fp32 input of a linear with a ConvRot group above 256 is rotated by the kernel
+    and multiplied by the dequantized weight (int8_gemv.py:49-57); a gated MLP runs one stacked gate|up linear
+    (:67-75). Both against float64 restatements."""
+    gv = pkg.int8_gemv
+    g = np.random.default_rng(6)
+    T, K, N, F_ = 5, 1024, 256, 512
+    w = g.integers(-127, 128, (N, K), dtype=np.int8)
+    s = (g.random(N) * 1e-3).astype(F32)
+    x = g.standard_normal((1, T, K)).astype(F32)
+    lin = _int8_linear(w, s, dev)
+    wg = g.integers(-127, 128, (F_, K), dtype=np.int8)
+    wu = g.integers(-127, 128, (F_, K), dtype=np.int8)
+    sg, su = (g.random(F_) * 1e-3).astype(F32), (g.random(F_) * 1e-3).astype(F32)
+    down_seen = []
+    mlp = types.SimpleNamespace(gate_proj=_int8_linear(wg, sg, dev), up_proj=_int8_linear(wu, su, dev),
+                                activation=torch.nn.functional.silu, down_proj=lambda h: down_seen.append(h) or h)
+    gv.generating = True
+    try:
+        got = gv.linear_forward(lin, N, K, torch.int8, 1024, dev_(x, dev)).cpu().numpy()
+        got_mlp = gv.mlp_forward(mlp, torch.int8, dev_(x, dev)).cpu().numpy()
+    finally:
+        gv.generating = False
+    xr = odec.rotate(x.reshape(-1), 1024).reshape(T, K).astype(np.float64)
+    ref = xr @ (w.astype(np.float64) * s[:, None]).T
+    assert got.shape == (1, T, N) and oatt.rel_l2(got.reshape(T, N), ref) < 1e-5
+    x64 = x.reshape(T, K).astype(np.float64)
+    gate = x64 @ (wg.astype(np.float64) * sg[:, None]).T
+    up = x64 @ (wu.astype(np.float64) * su[:, None]).T
+    ref_h = gate / (1 + np.exp(-gate)) * up
+    assert len(down_seen) == 1 and oatt.rel_l2(got_mlp.reshape(T, F_), ref_h) < 1e-5
 
 
 def test_linear_forward_drop_in(pkg, dev):
