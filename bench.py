@@ -612,6 +612,74 @@ class DecodeC5:
         return dt * 1e3, "4 of 36 layers through the reference's F.linear(x, w.float() * scale) fallback + fp32 softmax attention, scaled to 36 layers"
 
 
+class LogitsC5:
+    """The logits of one decode step: the tied bf16 embedding table of the C5 decoder's family (vocab 151936 x 2560,
+    778 MB, larger than L2) against one fp32 hidden state (int8_gemv.py:87-98)."""
+    name = "logits"
+    metric = "LM-head logits GEMV GB/s (bf16 table 151936 x 2560, one fp32 token)"
+    unit = "GB/s"
+    higher = True
+    N, K = 151936, 2560
+
+    def __init__(self, dev):
+        p = pkg()
+        self.ops = p.ops
+        g = torch.Generator().manual_seed(7)
+        self.table = (torch.randn((self.N, self.K), generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        self.x_host = torch.randn((self.K,), generator=g).pin_memory()
+        self.x = self.x_host.to(dev)
+        self.out = torch.empty((self.N,), dtype=torch.float32, device=dev)
+        self.out_host = torch.empty((self.N,), dtype=torch.float32).pin_memory()
+        self.bytes = self.N * self.K * 2 + self.K * 4 + self.N * 4
+        self.events = []
+        self.launches_per_step = 1
+        self.config = {"workload": "C5 logits (tied bf16 embedding table)", "N": self.N, "K": self.K,
+                       "l2": "778 MB table per step, larger than L2"}
+
+    def step(self, i, record=False):
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.ops.gemv_bf16(self.x, self.table, out=self.out)
+        if record:
+            e1.record()
+            self.events.append((e0, e1))
+
+    def e2e_step(self, i):
+        self.x.copy_(self.x_host, non_blocking=True)
+        self.ops.gemv_bf16(self.x, self.table, out=self.out)
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    h2d_bytes = property(lambda self: self.K * 4)
+    d2h_bytes = property(lambda self: self.N * 4)
+
+    def value(self, ms, steps, world):
+        return self.bytes * steps * world / (ms * 1e-3) / 1e9
+
+    def roofline(self, peaks, kms):
+        achieved = self.bytes / (kms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC.get("logits"), "kernel": "gemv_bf16_kernel",
+                "note": f"{peaks['source']} HBM copy bandwidth"}
+
+    @staticmethod
+    def cpu_baseline(threads):
+        """The transformer's own logits on the host: F.linear(x, table.float()) on a 16384-row slice, scaled."""
+        import torch.nn.functional as Fn
+
+        torch.set_num_threads(threads)
+        g = torch.Generator().manual_seed(7)
+        rows = 16384
+        table = (torch.randn((rows, LogitsC5.K), generator=g) * 0.02).to(torch.bfloat16)
+        x = torch.randn((1, LogitsC5.K), generator=g)
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            Fn.linear(x, table.float())
+        dt = (time.perf_counter() - t0) / reps * LogitsC5.N / rows
+        return (LogitsC5.N * LogitsC5.K * 2) / dt / 1e9, "16384 of 151936 rows, F.linear(x, table.float()), scaled"
+
+
 class KindTimer:
     """Records CUDA events around each launch of a kind ("gemm", "attention", ...) during one instrumented step."""
 
@@ -802,7 +870,8 @@ class DiTC4:
 
 
 WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4,
-             "w4a8": W4A8C3, "gemm_qkv": GemmQKV, "prepass": PrepassC4, "decode": DecodeC5}
+             "w4a8": W4A8C3, "gemm_qkv": GemmQKV, "prepass": PrepassC4, "decode": DecodeC5,
+             "logits": LogitsC5}
 
 
 def reference_arm(args, world, rank):
@@ -827,6 +896,10 @@ def reference_arm(args, world, rank):
         v, sample = DecodeC5.cpu_baseline(threads)
         metric, unit, higher = DecodeC5.metric, DecodeC5.unit, False
         cfg = {"workload": "C5 single-token decode", "layers": 36, "hidden": 2560, "kv_len": 1024}
+    elif name == "logits":
+        v, sample = LogitsC5.cpu_baseline(threads)
+        metric, unit, higher = LogitsC5.metric, LogitsC5.unit, True
+        cfg = {"workload": "C5 logits (tied bf16 embedding table)", "N": LogitsC5.N, "K": LogitsC5.K}
     elif name == "dit":
         v, sample = DiTC4.cpu_baseline(threads)
         metric, unit, higher = DiTC4.metric, DiTC4.unit, False

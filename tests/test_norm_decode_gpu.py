@@ -92,7 +92,7 @@ def test_gemv_i8(pkg, dev, N, K):
         assert oatt.rel_l2(got.cpu().numpy(), ref) < 1e-5
 
 
-@pytest.mark.parametrize("N,K", [(151936, 2560), (4096, 2560), (16, 256), (37, 264), (5, 8), (1000, 1288)])
+@pytest.mark.parametrize("N,K", [(151936, 256), (4096, 2560), (16, 256), (37, 264), (5, 8), (1000, 1288)])
 def test_gemv_bf16(pkg, dev, N, K):
     """The logits GEMV on a bf16 table, including ragged K (a partial last 256-value step) and N off the 16-row CTA."""
     g = np.random.default_rng(N * 7 + K)
