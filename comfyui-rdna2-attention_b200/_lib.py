@@ -26,6 +26,7 @@ SIGNATURES = {
     "b2_quant_pack_a_seg": (I, [P, I64, I, I64, P, P, I, I, I, P]),
     "b2_swiglu_quant_pack_a": (I, [P, P, I64, P, P, I, I, I, P, P]),
     "b2_gate_quant_pack_a": (I, [P, P, I64, P, P, I, I, I, P, P]),
+    "b2_situ_quant_pack_a": (I, [P, I64, P, P, I, I, I, P, P]),
     "b2_mod_quant_pack_a": (I, [P, I64, P, P, P, I, F, P, P, I, I, I, P, P]),
     "b2_gemm": (I, [P, P, P, P, P, P, I, I, I, P, P, I, P]),
     "b2_gemm_i32": (I, [P, P, P, I, I, I, P]),

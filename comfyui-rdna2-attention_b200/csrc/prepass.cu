@@ -7,6 +7,8 @@
 //   SwiGLU       : fp16(fp16(g / (1 + exp(-g))) * u)                                                (:129-132)
 //   sigmoid gate : fp16(x * fp16(1 / (1 + exp(-g))))                                                (:134-137)
 //   modulate     : fp16(fp16(fp16(x * rstd * (w + 1)) * s) + t), no contraction                     (:139-143)
+//   situ         : fp16(4 tanh(g / 4) sigmoid(g) 25 tanh(h / 25)) of a [h | g] row, tanh and sigmoid from
+//                  base-2 exponentials, one rounding at the end                                       (:118-127,:202)
 // The block-128 rotation (the configuration's normalised Hadamard) is Sylvester H2^(x)7, one bit at a
 // time from bit 0, butterflies (a+b, a-b), then y = fp16(v * fp32(1/sqrt(128))).
 //
@@ -22,7 +24,10 @@
 namespace b2 {
 namespace {
 
-enum Act { ACT_NONE = 0, ACT_SWIGLU = 1, ACT_GATE = 2, ACT_MOD = 3 };
+enum Act { ACT_NONE = 0, ACT_SWIGLU = 1, ACT_GATE = 2, ACT_MOD = 3, ACT_SITU = 4 };
+
+template <int ACT>
+__host__ __device__ constexpr bool two_inputs() { return ACT == ACT_SWIGLU || ACT == ACT_GATE || ACT == ACT_SITU; }
 
 constexpr int PP_WARPS = 4;
 constexpr int T_FLOATS = 576;  // 32 x 16 transpose plus bank padding
@@ -134,6 +139,34 @@ __device__ __forceinline__ float sigmoid_gate(float x, float g) {
     const float sig = round_h(__fdividef(1.f, __fadd_rn(1.f, __expf(-g))));
     return round_h(__fmul_rn(x, sig));
 }
+
+// tanh(x) = (1 - t) / (1 + t) with t = 2^(-2 |x| log2(e)), and its odd series x (1 - x^2 (1/3 - x^2 2/15)) below
+// |x| = 0.02, where 1 - t would cancel (int8_gemm.hip:118-122).
+__device__ __forceinline__ float soft_tanh(float x) {
+    const float ax = fabsf(x);
+    float y;
+    if (ax < 0.02f) {
+        const float a2 = __fmul_rn(ax, ax);
+        y = __fmul_rn(ax, __fsub_rn(1.f, __fmul_rn(a2, __fsub_rn(1.f / 3.f, __fmul_rn(a2, 2.f / 15.f)))));
+    } else {
+        const float t = ex2_approx(__fmul_rn(-2.885390082f, ax));
+        y = __fdiv_rn(__fsub_rn(1.f, t), __fadd_rn(1.f, t));
+    }
+    return x < 0.f ? -y : y;
+}
+
+// The situ activation of a [hidden | gate] pair, soft-capped: fp16(4 tanh(g / 4) sigmoid(g) 25 tanh(h / 25)), the
+// products taken left to right (int8_gemm.hip:124-127).
+__device__ __forceinline__ float situ(float h, float g) {
+    const float sig = __fdiv_rn(1.f, __fadd_rn(1.f, ex2_approx(__fmul_rn(-1.442695041f, g))));
+    const float a = __fmul_rn(__fmul_rn(4.f, soft_tanh(__fmul_rn(g, 0.25f))), sig);
+    return round_h(__fmul_rn(__fmul_rn(a, 25.f), soft_tanh(__fmul_rn(h, 0.04f))));
+}
+
+__device__ __forceinline__ uint32_t situ_h2(uint32_t h2, uint32_t g2) {
+    const float2 h = __half22float2(u32_as_h2(h2)), g = __half22float2(u32_as_h2(g2));
+    return h2_as_u32(__floats2half2_rn(situ(h.x, g.x), situ(h.y, g.y)));
+}
 __device__ __forceinline__ float modulate(float x, float rstd, float w, float s, float t) {
     const float n = round_h(__fmul_rn(__fmul_rn(x, rstd), __fadd_rn(w, 1.f)));
     return round_h(__fadd_rn(round_h(__fmul_rn(n, s)), t));
@@ -229,7 +262,7 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
     const int k0 = (tid >> 2) * 128 + s * 8;
     float* T = reinterpret_cast<float*>(smem + warp * R128_WARP_BYTES);
     unsigned char* B8 = smem + warp * R128_WARP_BYTES + 4096;
-    constexpr bool TWO = ACT == ACT_SWIGLU || ACT == ACT_GATE;
+    constexpr bool TWO = two_inputs<ACT>();
 
     uint4 rx[4], ru[4];
     auto load_row = [&](int r) {
@@ -300,6 +333,8 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
                     } else if (ACT == ACT_GATE) {
                         const uint32_t sig = f2_to_h2(sigmoid2(h2_to_f2(uw[p])));
                         y[o][p] = h2_as_u32(__hmul2_rn(u32_as_h2(xw[p]), u32_as_h2(sig)));
+                    } else if (ACT == ACT_SITU) {
+                        y[o][p] = situ_h2(xw[p], uw[p]);
                     } else {
                         y[o][p] = xw[p];
                     }
@@ -489,14 +524,14 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
         __syncwarp();
     }
 
-    const __half* ur = (ACT == ACT_SWIGLU || ACT == ACT_GATE) ? a.u + (int64_t)row * a.ldu : nullptr;
+    const __half* ur = two_inputs<ACT>() ? a.u + (int64_t)row * a.ldu : nullptr;
     const __half* srow = ACT == ACT_MOD ? a.s + (int64_t)(row / a.L) * K : nullptr;
     const __half* trow = ACT == ACT_MOD ? a.t + (int64_t)(row / a.L) * K : nullptr;
 
     __half2 mx2 = __float2half2_rn(0.f);  // running max of |y| over this lane's values (fp16, exact)
     const int npass = (K + 511) >> 9;
     // Loads for PF passes are issued together, so each warp keeps PF KB (x2 with a second input) in flight.
-    constexpr bool TWO = ACT == ACT_SWIGLU || ACT == ACT_GATE;
+    constexpr bool TWO = two_inputs<ACT>();
     constexpr int PF = ACT == ACT_MOD ? 1 : (TWO ? 2 : 4);
     for (int p0 = 0; p0 < npass; p0 += PF) {
     uint4 rx[PF][2], ru[PF][2];
@@ -558,7 +593,10 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
                     float u[16];
                     unpack16(ru[j], u);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) v[i] = ACT == ACT_SWIGLU ? silu_mul(v[i], u[i]) : sigmoid_gate(v[i], u[i]);
+                    for (int i = 0; i < 16; i++)
+                        v[i] = ACT == ACT_SWIGLU ? silu_mul(v[i], u[i])
+                             : ACT == ACT_GATE   ? sigmoid_gate(v[i], u[i])
+                                                 : situ(v[i], u[i]);
                 }
             }
             if (ACT != ACT_NONE && a.act_out) store16(a.act_out + (int64_t)row * K + k0, v);
@@ -790,6 +828,19 @@ extern "C" int b2_gate_quant_pack_a(const uint16_t* x, const uint16_t* gate, int
     if (int rc = validate(a, rot_group)) return rc;
     if (M == 0) return B2_OK;
     return launch_rot<ACT_GATE>(a, rot_group, (cudaStream_t)stream);
+}
+
+extern "C" int b2_situ_quant_pack_a(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
+                                    uint16_t* act_out, void* stream) {
+    // Row m is [hidden (K values) | gate (K values)] at x + m * ldx.
+    PrepassArgs a = base_args(x, ldx, q, scale, M, K);
+    a.u = x ? reinterpret_cast<const __half*>(x) + K : nullptr;
+    a.ldu = ldx;
+    a.act_out = reinterpret_cast<__half*>(act_out);
+    if (int rc = validate(a, rot_group)) return rc;
+    if (ldx < 2 * (int64_t)K) return fail(B2_ERR_INVALID, "situ: row stride %lld below 2K = %d", (long long)ldx, 2 * K);
+    if (M == 0) return B2_OK;
+    return launch_rot<ACT_SITU>(a, rot_group, (cudaStream_t)stream);
 }
 
 extern "C" int b2_mod_quant_pack_a(const uint16_t* x, int64_t ldx, const float* w, const uint16_t* s, const uint16_t* t,

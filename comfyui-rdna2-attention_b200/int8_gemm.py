@@ -41,15 +41,21 @@ def quantized(M, K, device):
     return (torch.empty((M, K), dtype=torch.int8, device=device), torch.empty((M,), dtype=torch.float32, device=device))
 
 
-def run(x, weight, weight_scale, bias, rotate=False, up=None, gate=None, activations=None, res=None, rot_group=ROT_GROUP):
-    """Pre-pass (unless ``activations`` are given) then GEMM. x (M, K) fp16; weight (N, K) int8; weight_scale (N,)
-    fp32; res = (R (M, N) fp16, G (M / L, N) fp16) adds R + G * y. Returns (M, N) fp16 (int8_gemm.py:56-80)."""
+def run(x, weight, weight_scale, bias, rotate=False, up=None, gate=None, activations=None, res=None, rot_group=ROT_GROUP,
+        situ=False):
+    """Pre-pass (unless ``activations`` are given) then GEMM. x (M, K) fp16, or (M, 2K) [hidden | gate] with situ;
+    weight (N, K) int8; weight_scale (N,) fp32; res = (R (M, N) fp16, G (M / L, N) fp16) adds R + G * y. Returns
+    (M, N) fp16 (int8_gemm.py:56-80)."""
     M = x.shape[0] if activations is None else activations[0].shape[0]
     N, K = weight.shape
-    group = rot_group if rotate else 0
+    group = rot_group if rotate or situ else 0
     if activations is None:
         out = quantized(M, K, x.device)
-        if up is not None:
+        if situ:
+            if x.shape[1] != 2 * K:
+                raise RuntimeError(f"situ input width {x.shape[1]} is not 2 x K = {2 * K}")
+            activations = ops.situ_quant_pack_a(x, group, out=out)
+        elif up is not None:
             activations = ops.swiglu_quant_pack_a(x, up, group, out=out)
         elif gate is not None:
             activations = ops.gate_quant_pack_a(x, gate, group, out=out)
@@ -66,11 +72,11 @@ def run(x, weight, weight_scale, bias, rotate=False, up=None, gate=None, activat
 
 def linear(x, weight, weight_scale, bias, rotate=False, situ=False, up=None, gate=None, activations=None, res=None,
            rot_group=ROT_GROUP):
-    """x is (M, K) fp16, weight (N, K) int8 and weight_scale (N,) fp32. With up, x is the gate of a SwiGLU. With gate,
-    x is multiplied by its sigmoid. Returns (M, N) fp16 (int8_gemm.py:83-87)."""
-    if situ:
-        raise NotImplementedError("the situ (Anima) activation is not part of this build's pre-pass")
-    return run(x, weight, weight_scale, bias, rotate, up, gate, activations, res, rot_group)
+    """x is (M, K) fp16, or (M, 2K) with situ, weight (N, K) int8 and weight_scale (N,) fp32. With up, x is the gate
+    of a SwiGLU. With gate, x is multiplied by its sigmoid. With situ, x's rows are [hidden | gate] and the pre-pass
+    applies the situ activation, then ConvRot (situ layers always rotate: int8_gemm.py:152-157 only hands over layers
+    that do). Returns (M, N) fp16 (int8_gemm.py:83-87)."""
+    return run(x, weight, weight_scale, bias, rotate, up, gate, activations, res, rot_group, situ)
 
 
 def ineligible(x, weight, bias, compute_dtype, x_q):
@@ -135,6 +141,16 @@ def fuse_act(layer, x, K):
             and getattr(layer, "_convrot_groupsize", 0) == ROT_GROUP and not getattr(layer, "lora_patches", None)
             and x.dtype == torch.float16 and K == layer.in_features and layer.in_features % ROT_GROUP == 0
             and layer.in_features <= MAX_ROT_K)
+
+
+def linear_input_act(linear, x, input_act, act_weight=None, act_eps=0.0, residual=None, residual_scale=None):
+    """comfy.ops.linear_input_act for situ layers (int8_gemm.py:152-157): the raw [hidden | gate] input goes to the
+    linear, whose pre-pass applies the activation, so the K-wide activation never goes through HBM."""
+    global situ_next
+    if input_act == "situ" and residual is None and fuse_act(linear, x, x.shape[-1] // 2):
+        situ_next = True
+        return linear(x)
+    return originals["linear_input_act"](linear, x, input_act, act_weight, act_eps, residual, residual_scale)
 
 
 def swiglu_forward(module, x):
@@ -236,6 +252,10 @@ def enable(on):
                          triton_int8_linear_per_row=pack.triton_int8_linear_per_row,
                          rotate_activation=convrot.rotate_activation, build_hadamard=convrot.build_hadamard,
                          forward=layer.forward)
+    comfy_ops = sys.modules.get("comfy.ops")
+    if comfy_ops is not None and hasattr(comfy_ops, "linear_input_act"):
+        originals.setdefault("linear_input_act", comfy_ops.linear_input_act)
+        comfy_ops.linear_input_act = linear_input_act if on else originals["linear_input_act"]
     for name in ("triton_int8_linear", "triton_int8_linear_per_row"):
         setattr(pack, name, wrap(originals[name]) if on else originals[name])
     convrot.rotate_activation = rotate_activation if on else originals["rotate_activation"]

@@ -66,6 +66,22 @@ def gate_quant_pack_a(x, gate, rot_group=ROT_NONE, act_out=None, out=None):
     return q, s
 
 
+def situ_quant_pack_a(x, rot_group=ROT_NONE, act_out=None, out=None):
+    """int8 of the situ activation fp16(4 tanh(g/4) sigmoid(g) 25 tanh(h/25)) after an optional rotation. x fp16
+    [M, 2K] holds [h | g] per row; the result is [M, K]."""
+    require_cuda(x)
+    _half2d(x, "x")
+    M, K2 = x.shape
+    if K2 % 2:
+        raise RuntimeError("situ input rows must be [hidden | gate], an even width")
+    K = K2 // 2
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=x.device),
+                                        torch.empty((M,), dtype=torch.float32, device=x.device))
+    call("b2_situ_quant_pack_a", ptr(x), I64(x.stride(0)), ptr(q), ptr(s), I(M), I(K), I(rot_group), ptr(act_out),
+         stream())
+    return q, s
+
+
 def mod_quant_pack_a(x, weight, s_rows, t_rows, L, eps, rot_group=ROT_NONE, act_out=None, out=None):
     """int8 of the modulated RMSNorm fp16(fp16(fp16(x*rstd*(w+1)) * s) + t) after an optional rotation.
     x fp16 [M, K]; weight fp32 [K]; s_rows (= 1 + scale), t_rows fp16 [M // L, K]."""

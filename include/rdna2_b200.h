@@ -72,6 +72,10 @@ int b2_swiglu_quant_pack_a(const uint16_t* gate, const uint16_t* up, int64_t ld,
 /* h = fp16(x * fp16(sigmoid(gate))), as x * F.sigmoid(gate) (int8_gemm.hip:134-137). */
 int b2_gate_quant_pack_a(const uint16_t* x, const uint16_t* gate, int64_t ld, int8_t* q, float* scale, int M, int K,
                          int rot_group, uint16_t* act_out, void* stream);
+/* h = fp16(4 tanh(g / 4) sigmoid(g) 25 tanh(h / 25)) of rows [h (K) | g (K)] at x + m * ldx, ldx >= 2K
+ * (int8_gemm.hip:118-127 situ, situ_rot_quant_pack_a :249; caller int8_gemm.py:83-87,152-157). */
+int b2_situ_quant_pack_a(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
+                         uint16_t* act_out, void* stream);
 /* h = fp16(fp16(fp16(x * rstd * (w + 1)) * s) + t), rstd = rsqrt(mean(x^2) + eps); s (= 1 + scale)
  * and t are fp16 [M / L, K] rows (int8_gemm.hip:139-143,167-191; caller int8_gemm.py:176-186). */
 int b2_mod_quant_pack_a(const uint16_t* x, int64_t ldx, const float* w, const uint16_t* s, const uint16_t* t, int L,

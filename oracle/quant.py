@@ -99,6 +99,31 @@ def sigmoid_gate(x, gate):
     return (xf * sig).astype(F16)
 
 
+def soft_tanh(x):
+    """tanh through base-2 exponentials as int8_gemm.hip:118-122: ax = |x|, t = 2^(-2.885390082 ax),
+    y = (1 - t) / (1 + t), or ax (1 - ax^2 (1/3 - ax^2 2/15)) below ax = 0.02; the sign of x restored."""
+    x = np.asarray(x, F32)
+    ax = np.abs(x)
+    with np.errstate(over="ignore", invalid="ignore"):
+        t = np.exp2(F32(-2.885390082) * ax).astype(F32)
+        y = ((F32(1) - t) / (F32(1) + t)).astype(F32)
+    a2 = ax * ax
+    series = ax * (F32(1) - a2 * (F32(1) / F32(3) - a2 * (F32(2) / F32(15))))
+    y = np.where(ax < F32(0.02), series, y).astype(F32)
+    return np.where(x < 0, -y, y).astype(F32)
+
+
+def situ(hidden, gate):
+    """fp16(4 tanh(g / 4) sigmoid(g) 25 tanh(h / 25)), the products left to right and sigmoid through 2^x
+    (int8_gemm.hip:124-127)."""
+    h = np.asarray(hidden).astype(F32)
+    g = np.asarray(gate).astype(F32)
+    with np.errstate(over="ignore"):
+        sig = (F32(1) / (F32(1) + np.exp2(F32(-1.442695041) * g))).astype(F32)
+    a = (F32(4) * soft_tanh(g * F32(0.25))) * sig
+    return ((a * F32(25)) * soft_tanh(h * F32(0.04))).astype(F16)
+
+
 def rms_rstd(x):
     """rsqrt(sum(x^2) / K + eps) per row in fp32 (int8_gemm.hip:167-189; the sum order is not reproduced)."""
     f = np.asarray(x).astype(F32)
@@ -130,6 +155,10 @@ def prepass(x, rot_group, act="none", u=None, w=None, s=None, t=None, L=1, eps=1
         a16 = sigmoid_gate(x, u)
     elif act == "mod":
         a16 = modulate(x, w, s, t, L, eps)
+    elif act == "situ":
+        xs = np.asarray(x)
+        k = xs.shape[1] // 2
+        a16 = situ(xs[:, :k], xs[:, k:])
     else:
         raise ValueError(act)
     y16 = rotate_rows(a16, rot_group)

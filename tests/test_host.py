@@ -63,6 +63,9 @@ def test_validation_errors_before_any_launch(pkg):
     assert _status(pkg, "b2_gemv_i8_ex", fake, fake, fake, P(None), fake, fake, I(8), I(16), I(0), P(None)) == 1
     assert _status(pkg, "b2_decode_qk_rope", fake, fake, fake, fake, P(None), fake, fake, fake, I(8), I(2), F(1e-6),
                    P(None)) == 1
+    # situ: the row stride must hold [hidden | gate]
+    assert _status(pkg, "b2_situ_quant_pack_a", fake, I64(256), fake, fake, I(4), I(256), I(0), P(None), P(None)) == 1
+    assert _status(pkg, "b2_situ_quant_pack_a", fake, I64(520), fake, fake, I(4), I(260), I(0), P(None), P(None)) == 2
     # bf16 GEMV: K % 8, null table
     assert _status(pkg, "b2_gemv_bf16", fake, fake, fake, I(16), I(12), P(None)) == 2
     assert _status(pkg, "b2_gemv_bf16", fake, P(None), fake, I(16), I(16), P(None)) == 1

@@ -97,6 +97,25 @@ def test_swiglu_and_gate_round_at_torch_points():
     assert np.mean(oq.sigmoid_gate(up, gate) != ref_g) < 1e-2
 
 
+def test_situ_is_soft_capped_gated_tanh():
+    """int8_gemm.hip:118-127: situ(h, g) = 4 tanh(g/4) sigmoid(g) 25 tanh(h/25), tanh and sigmoid via 2^x with the
+    odd series below |x| = 0.02; one fp16 rounding. Against float64 math: within one fp16 step; odd in h; bounded by
+    100 in magnitude; the series and exponential branches of tanh meet within an fp32 ulp."""
+    g = np.random.default_rng(9)
+    h = (g.standard_normal(4096) * 60).astype(F16)
+    gt = (g.standard_normal(4096) * 4).astype(F16)
+    got = oq.situ(h, gt).astype(np.float64)
+    h64, g64 = h.astype(np.float64), gt.astype(np.float64)
+    exact = 4 * np.tanh(g64 / 4) / (1 + np.exp(-g64)) * 25 * np.tanh(h64 / 25)
+    assert np.all(np.abs(got - exact) <= np.abs(np.spacing(exact.astype(F16))).astype(np.float64))
+    assert np.array_equal(oq.situ(-h, gt), -oq.situ(h, gt))
+    assert np.all(np.abs(got) < 100)
+    edge = np.array([np.nextafter(F32(0.02), F32(0)), F32(0.02)], F32)
+    assert abs(float(oq.soft_tanh(edge)[0]) - float(oq.soft_tanh(edge)[1])) < 2 * float(np.spacing(F32(0.02)))
+    q, s, a = oq.prepass(np.concatenate([h.reshape(16, 256), gt.reshape(16, 256)], axis=1), 256, act="situ")
+    assert a.shape == (16, 256) and np.array_equal(a, oq.situ(h.reshape(16, 256), gt.reshape(16, 256)))
+
+
 def test_modulate_with_identity_modulation_is_rms_norm():
     g = np.random.default_rng(5)
     x = g.standard_normal((6, 256)).astype(F16)

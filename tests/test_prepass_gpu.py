@@ -133,3 +133,38 @@ def test_mod_prepass(pkg, dev, rot):
     ref = oq.modulate(x, w, s_rows, t_rows, L, 1e-6)
     mag = np.abs(ref.astype(np.float32)) + np.abs(np.repeat(t_rows, L, axis=0).astype(np.float32))
     _check_act(pkg, dev, act, ref, q, s, rot, mag=mag)
+
+
+@pytest.mark.parametrize("rot", [0, 128, 256])
+@pytest.mark.parametrize("M,K", [(97, 3072), (33, 640)])
+def test_situ_prepass(pkg, dev, rot, M, K):
+    """situ on [hidden | gate] rows (int8_gemm.hip:118-127): the fp16 activation within two steps of the float32
+    restatement (base-2 exponentials differ by an ulp), then int8 bit-exact from the kernel's own activation. Hidden
+    values reach the soft cap (|h| up to ~100), gates cross the series branch of tanh (|g / 4| < 0.02)."""
+    if rot and K % rot:
+        pytest.skip("K not a multiple of the rotation group")
+    g = np.random.default_rng(M + K)
+    h = (g.standard_normal((M, K)) * 30).astype(F16)
+    gt = (g.standard_normal((M, K)) * 3).astype(F16)
+    gt[:, :64] = (g.standard_normal((M, 64)) * 0.02).astype(F16)
+    x = np.concatenate([h, gt], axis=1)
+    act = torch.empty((M, K), dtype=torch.float16, device=dev)
+    q, s = pkg.ops.situ_quant_pack_a(dev_(x, dev), rot, act_out=act)
+    _check_act(pkg, dev, act, oq.situ(h, gt), q, s, rot)
+
+
+def test_situ_linear_drop_in(pkg, dev):
+    """int8_gemm.linear(situ=True): [hidden | gate] rows -> situ -> ConvRot -> int8 -> GEMM, bit-exact against the
+    oracle's pre-pass of the kernel's activation and the epilogue restatement."""
+    from oracle import gemm as ogemm
+
+    M, K, N = 130, 1024, 264
+    g = np.random.default_rng(21)
+    x = np.concatenate([(g.standard_normal((M, K)) * 10).astype(F16), g.standard_normal((M, K)).astype(F16)], axis=1)
+    wq = g.integers(-127, 128, (N, K), dtype=np.int8)
+    ws = (g.random(N) * 1e-3).astype(np.float32)
+    y = pkg.int8_gemm.linear(dev_(x, dev), dev_(wq, dev), dev_(ws, dev), None, situ=True).cpu().numpy()
+    act = torch.empty((M, K), dtype=torch.float16, device=dev)
+    pkg.ops.situ_quant_pack_a(dev_(x, dev), 256, act_out=act)
+    q_ref, s_ref = oq.quant_rows(oq.rotate_rows(act.cpu().numpy(), 256))
+    assert np.array_equal(y, ogemm.epilogue(ogemm.int_mm(q_ref, wq), s_ref, ws))
