@@ -32,6 +32,9 @@ SIGNATURES = {
     "b2_gemm_i32": (I, [P, P, P, I, I, I, P]),
     "b2_gemm_swiglu": (I, [P, P, P, P, P, I, I, I, P]),
     "b2_gemm_w4a8": (I, [P, P, P, P, P, P, I, I, I, P]),
+    "b2_quant_pack_a_i4": (I, [P, I64, P, P, I, I, I, P]),
+    "b2_unpack_int4": (I, [P, P, I, I, P]),
+    "b2_gemm_w4a4": (I, [P, P, P, P, P, P, I, I, I, P, P]),
     "b2_attention_workspace_bytes": (I64, [I, I, I, I, I, I]),
     "b2_attention": (I, [P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
                          I, I, I, I, I, F, I, P, I64, P]),

@@ -345,3 +345,61 @@ extern "C" int b2_gemm_w4a8(const int8_t* A, const uint8_t* Wp, const float* as,
     gemm_w4a8_kernel<<<grid, W4_THREADS, SMEM, (cudaStream_t)stream>>>(ta, tw, ts, g);
     return check_launch("gemm_w4a8_kernel");
 }
+
+// ---------------------------------------------------------------- per-channel W4A4
+// The reference's own int4 path (int8_gemm.hip:412 gemm_i4, int8_gemm.py:90-103): activations with int4 values
+// (b2_quant_pack_a_i4), int4 weights with one fp32 scale per output channel, int32 accumulation over all of K and
+// the W8A8 epilogue y = (float)acc * as[m] * ws[n] (+ bias[n]). tcgen05 has no integer int4 kind, so the packed
+// weight is widened to int8 into a caller-provided workspace by one streaming pass (as the reference re-packs its
+// weights per call, pack_b, int8_gemm.hip:270-276) and the W8A8 kernel runs on it; int32 sums are exact in any
+// order, so the result is the reference's bit for bit.
+namespace b2 {
+namespace {
+
+// Four nibble values b in [0, 15] (one per byte) -> two's-complement int8 bytes: (b ^ 8) - 8 per byte.
+__device__ __forceinline__ uint32_t sext_nibbles(uint32_t b) { return __vsub4(b ^ 0x08080808u, 0x08080808u); }
+
+// Packed byte j holds k = 2j (low nibble) and k = 2j + 1 (high nibble). Each thread widens 16 packed bytes (32
+// values) into two 16-byte stores.
+__global__ void __launch_bounds__(256) unpack_int4_kernel(const uint4* __restrict__ wp, uint4* __restrict__ w, int64_t n16) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint4 p = __ldg(wp + i);
+        const uint32_t in[4] = {p.x, p.y, p.z, p.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = in[j] & 0x0F0F0F0Fu, hi = (in[j] >> 4) & 0x0F0F0F0Fu;
+            o[2 * j] = sext_nibbles(__byte_perm(lo, hi, 0x5140));      // k = 8j .. 8j + 3
+            o[2 * j + 1] = sext_nibbles(__byte_perm(lo, hi, 0x7362));  // k = 8j + 4 .. 8j + 7
+        }
+        w[2 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+        w[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_unpack_int4(const uint8_t* Wp, int8_t* W, int N, int K, void* stream) {
+    if (!Wp || !W || N < 0 || K <= 0) return fail(B2_ERR_INVALID, "unpack_int4: bad arguments");
+    if (K % 32) return fail(B2_ERR_UNSUPPORTED, "unpack_int4: K=%d must be a multiple of 32", K);
+    if (!aligned16(Wp) || !aligned16(W)) return fail(B2_ERR_UNSUPPORTED, "unpack_int4: Wp and W must be 16-byte aligned");
+    const int64_t n16 = (int64_t)N * (K / 32);
+    if (n16 == 0) return B2_OK;
+    const int64_t blocks = (n16 + 255) / 256;
+    const int cap = sm_count() * 8;
+    unpack_int4_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint4*>(Wp), reinterpret_cast<uint4*>(W), n16);
+    return check_launch("unpack_int4_kernel");
+}
+
+extern "C" int b2_gemm_w4a4(const int8_t* A, const uint8_t* Wp, const float* as, const float* ws, const uint16_t* bias,
+                            uint16_t* C, int M, int N, int K, int8_t* workspace, void* stream) {
+    if (!A || !Wp || !as || !ws || !C || !workspace) return fail(B2_ERR_INVALID, "gemm_w4a4: null pointer");
+    if (M < 0 || N <= 0 || K <= 0) return fail(B2_ERR_INVALID, "gemm_w4a4: bad shape M=%d N=%d K=%d", M, N, K);
+    if (K % 32) return fail(B2_ERR_UNSUPPORTED, "gemm_w4a4: K=%d must be a multiple of 32", K);
+    if (N % 8) return fail(B2_ERR_UNSUPPORTED, "gemm_w4a4: N=%d must be a multiple of 8", N);
+    if (M == 0) return B2_OK;
+    if (int rc = b2_unpack_int4(Wp, workspace, N, K, stream)) return rc;
+    return b2_gemm(A, workspace, as, ws, bias, C, M, N, K, nullptr, nullptr, 1, stream);
+}

@@ -189,6 +189,13 @@ __device__ __forceinline__ void park16(__half* p, const float (&v)[16], float c,
 // floor(f / scale + 0.5) with the IEEE quotient, computed as f * (1/scale): |f / scale| <= 127 keeps that product
 // within 2e-5 of the quotient, so unless f * inv + 0.5 lands within 1e-4 of an integer the floor is the same; those
 // few values take the IEEE divide. The result is bit-identical to floorf(f / scale + 0.5f).
+// W4A4 activations (int8_gemm.hip:62-91 quant_row_i4): q = clamp(rint(f / scale), -7, 7) with an IEEE divide,
+// kept here as one int8 per value; a NaN quotient clamps to -7 like fminf(fmaxf(NaN, -7), 7).
+__device__ __forceinline__ int quant1_i4(float f, float scale) {
+    const float r = fminf(fmaxf(rintf(__fdiv_rn(f, scale)), -7.f), 7.f);
+    return __float_as_int(__fadd_rn(r, 12582912.f)) - 0x4B400000;
+}
+
 __device__ __forceinline__ int quant1(float f, float scale, float inv) {
     const float u = __fmaf_rn(f, inv, 0.5f);
     float r = floorf(u);
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
     }
 }
 
-template <int ACT, int ROT>
+template <int ACT, int ROT, bool I4 = false>
 __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const PrepassArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -655,10 +662,12 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
     float mx = fmaxf(__low2float(mx2), __high2float(mx2));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float scale = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
+    // int8: max(absmax / 127, 1e-30) (int8_gemm.hip:38); int4 values: max(absmax, 1e-10) / 7 (:71).
+    const float scale = I4 ? __fdiv_rn(fmaxf(mx, 1e-10f), 7.f) : fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
     const float inv = __frcp_rn(scale);
     if (lane == 0) a.scale[row] = scale;
     __syncwarp();
+    auto qv = [&](float f) -> uint32_t { return (uint32_t)((I4 ? quant1_i4(f, scale) : quant1(f, scale, inv)) & 255); };
 
     // Each lane quantizes the 16 values it parked per pass. With a rotation they sit at transposed positions, so
     // the bytes go through a small shared-memory transpose (the float buffer, now free) and every lane then stores
@@ -678,10 +687,8 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
             for (int i = 0; i < 2; i++) {
                 const float2 a0 = __half22float2(h0[2 * i]), a1 = __half22float2(h0[2 * i + 1]);
                 const float2 b0 = __half22float2(h1[2 * i]), b1 = __half22float2(h1[2 * i + 1]);
-                w[i] = (uint32_t)(quant1(a0.x, scale, inv) & 255) | ((uint32_t)(quant1(a0.y, scale, inv) & 255) << 8) |
-                       ((uint32_t)(quant1(a1.x, scale, inv) & 255) << 16) | ((uint32_t)(quant1(a1.y, scale, inv) & 255) << 24);
-                w[2 + i] = (uint32_t)(quant1(b0.x, scale, inv) & 255) | ((uint32_t)(quant1(b0.y, scale, inv) & 255) << 8) |
-                           ((uint32_t)(quant1(b1.x, scale, inv) & 255) << 16) | ((uint32_t)(quant1(b1.y, scale, inv) & 255) << 24);
+                w[i] = qv(a0.x) | (qv(a0.y) << 8) | (qv(a1.x) << 16) | (qv(a1.y) << 24);
+                w[2 + i] = qv(b0.x) | (qv(b0.y) << 8) | (qv(b1.x) << 16) | (qv(b1.y) << 24);
             }
         }
         if (ROT == 0) {
@@ -732,20 +739,20 @@ int launch_r128(const PrepassArgs& a, cudaStream_t stream) {
     return check_launch("prepass128_kernel");
 }
 
-template <int ACT, int ROT>
+template <int ACT, int ROT, bool I4 = false>
 int launch_t(const PrepassArgs& a, cudaStream_t stream) {
-    if (ROT == 128 && a.K % 1024 == 0) return launch_r128<ACT>(a, stream);
+    if (!I4 && ROT == 128 && a.K % 1024 == 0) return launch_r128<ACT>(a, stream);
     const int smem = PP_WARPS * (a.K * 2 + T_BYTES);
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        int rc = set_smem(prepass_kernel<ACT, ROT>, PP_WARPS * (MAX_K * 2 + T_BYTES));
+        int rc = set_smem(prepass_kernel<ACT, ROT, I4>, PP_WARPS * (MAX_K * 2 + T_BYTES));
         if (rc) return rc;
         configured[dev] = true;
     }
     const int grid = (a.M + PP_WARPS - 1) / PP_WARPS;
-    prepass_kernel<ACT, ROT><<<grid, PP_WARPS * 32, smem, stream>>>(a);
+    prepass_kernel<ACT, ROT, I4><<<grid, PP_WARPS * 32, smem, stream>>>(a);
     return check_launch("prepass_kernel");
 }
 
@@ -804,6 +811,19 @@ extern "C" int b2_quant_pack_a_seg(const uint16_t* x, int64_t ldx, int seg, int6
 extern "C" int b2_quant_pack_a(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
                                void* stream) {
     return b2_quant_pack_a_seg(x, ldx, 0, 0, q, scale, M, K, rot_group, stream);
+}
+
+extern "C" int b2_quant_pack_a_i4(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
+                                  void* stream) {
+    PrepassArgs a = base_args(x, ldx, q, scale, M, K);
+    if (int rc = validate(a, rot_group)) return rc;
+    if (M == 0) return B2_OK;
+    switch (rot_group) {
+        case 0: return launch_t<ACT_NONE, 0, true>(a, (cudaStream_t)stream);
+        case 128: return launch_t<ACT_NONE, 128, true>(a, (cudaStream_t)stream);
+        case 256: return launch_t<ACT_NONE, 256, true>(a, (cudaStream_t)stream);
+        default: return fail(B2_ERR_UNSUPPORTED, "rot_group must be 0, 128 or 256 (got %d)", rot_group);
+    }
 }
 
 extern "C" int b2_swiglu_quant_pack_a(const uint16_t* gate, const uint16_t* up, int64_t ld, int8_t* q, float* scale,

@@ -10,7 +10,8 @@ Module globals are the same side channels as the reference's (:25-41).
 Differences, all by design of this build: every linear runs the sm_100a kernels (pre-pass + tcgen05 GEMM reading the
 weight as stored: no pack_b), for any row count, so MIN_ROWS is 1; inputs the kernels cannot take raise instead of
 falling back to the pack's Triton path; the rotation group is a parameter (256 = ConvRot as in the reference, 128 =
-the block-128 configuration).
+the block-128 configuration). ``wrap_w4a4`` runs the Int4 loader's per-channel W4A4 layers (int8_gemm.py:90-103) and
+``linear_input_act`` hands situ activations to the pre-pass (:152-157), as in the reference.
 """
 import functools
 import logging
@@ -111,12 +112,40 @@ def wrap(original):
     return int8_linear
 
 
+def w4a4_ineligible(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation, x_rot):
+    N, row_bytes = qweight.shape
+    K = row_bytes * 2
+    if x_rot is not None or skip_rotation:
+        return "a pre-rotated input (x_rot / skip_rotation)"
+    if convrot_groupsize != ROT_GROUP:
+        return f"ConvRot group {convrot_groupsize} (the W4A4 pre-pass rotates by {ROT_GROUP})"
+    if compute_dtype != torch.float16:
+        return "non-fp16 compute dtype"
+    if x.shape[-1] != K or K > MAX_ROT_K:
+        return f"input width {x.shape[-1]} against K = {K} (at most {MAX_ROT_K})"
+    if N % 8 or K % 256:
+        return f"N={N} must be a multiple of 8 and K={K} of 256"
+    if bias is not None and bias.dtype != torch.float16:
+        return "non-fp16 bias"
+    if wscales.numel() != N:
+        return "weight scales that are not one per output channel"
+    return None
+
+
 def wrap_w4a4(original):
-    """The reference runs the Int4 loader's W4A4 layers on gemm_i4 (int8_gemm.py:90-103). This build's int4 path is
-    W4A8 with group-128 scales (int4_gemm.py); per-channel W4A4 layers are not taken over."""
+    """convrot_w4a4_forward of the Int4 loader on the sm_100a kernels (int8_gemm.py:90-103): ConvRot-256 and
+    int4-valued per-token activations in one pre-pass, the packed weight widened to int8 and multiplied on the
+    tcgen05 int8 GEMM with int32 accumulation, the per-channel epilogue. Ineligible calls raise (no fallback)."""
     def convrot_w4a4_forward(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation=False,
                              qweight_unpacked=None, x_rot=None, orig_shape=None):
-        raise NotImplementedError("per-channel W4A4 layers are not supported by this build (W4A8 group-128 only)")
+        reason = w4a4_ineligible(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation, x_rot)
+        if reason:
+            raise NotImplementedError(f"convrot_w4a4_forward: {reason}")
+        N, K = qweight.shape[0], qweight.shape[1] * 2
+        x2d = x.reshape(-1, K).to(torch.float16).contiguous()
+        a_q, a_s = ops.quant_pack_a_i4(x2d, ROT_GROUP)
+        out = ops.gemm_w4a4(a_q, a_s, qweight.contiguous(), wscales.reshape(N).float().contiguous(), bias)
+        return out.reshape(x.shape[:-1] + (N,))
     return convrot_w4a4_forward
 
 

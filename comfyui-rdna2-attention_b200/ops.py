@@ -194,6 +194,58 @@ def gemm_w4a8(a_q, a_scale, w_packed, gscale, bias=None, out=None):
     return out
 
 
+def quant_pack_a_i4(x, rot_group=ROT_CONVROT, out=None):
+    """Per-row int4-valued activations of fp16 rows x [M, K] after an optional rotation: scale = max(absmax, 1e-10)
+    / 7, q = clamp(rint(y / scale), -7, 7), one int8 per value. Returns (int8 [M, K], fp32 [M])."""
+    require_cuda(x)
+    _half2d(x, "x")
+    M, K = x.shape
+    q, s = out if out is not None else (torch.empty((M, K), dtype=torch.int8, device=x.device),
+                                        torch.empty((M,), dtype=torch.float32, device=x.device))
+    call("b2_quant_pack_a_i4", ptr(x), I64(x.stride(0)), ptr(q), ptr(s), I(M), I(K), I(rot_group), stream())
+    return q, s
+
+
+def _packed_int4(w_packed, name):
+    if w_packed.dtype not in (torch.uint8, torch.int8) or w_packed.dim() != 2 or not w_packed.is_contiguous():
+        raise RuntimeError(f"{name}: the packed weight must be a contiguous 8-bit [N, K/2] tensor")
+
+
+def unpack_int4(w_packed, out=None):
+    """Packed int4 [N, K/2] (low nibble = even k, two's complement) -> int8 [N, K]."""
+    require_cuda(w_packed)
+    _packed_int4(w_packed, "unpack_int4")
+    N, K = w_packed.shape[0], w_packed.shape[1] * 2
+    out = torch.empty((N, K), dtype=torch.int8, device=w_packed.device) if out is None else out
+    call("b2_unpack_int4", ptr(w_packed), ptr(out), I(N), I(K), stream())
+    return out
+
+
+def gemm_w4a4(a_q, a_scale, w_packed, w_scale, bias=None, out=None, workspace=None):
+    """Per-channel W4A4: fp16 [M, N] = int32 (a_q . w^T) * a_scale[m] * w_scale[n] (+ bias), a_q int8 [M, K] with
+    int4 values, w_packed [N, K/2]. ``workspace`` (int8, N * K bytes) receives the widened weight; allocated here
+    when not given."""
+    require_cuda(a_q, a_scale, w_packed, w_scale, bias)
+    _packed_int4(w_packed, "gemm_w4a4")
+    M, K = a_q.shape
+    N = w_packed.shape[0]
+    if a_q.dtype != torch.int8 or w_packed.shape[1] * 2 != K or not a_q.is_contiguous():
+        raise RuntimeError("gemm_w4a4 operands must be contiguous int8 [M, K] and packed [N, K/2]")
+    if w_scale.dtype != torch.float32 or w_scale.numel() != N or not w_scale.is_contiguous():
+        raise RuntimeError("gemm_w4a4 weight scale must be contiguous fp32 [N]")
+    if bias is not None and (bias.dtype != torch.float16 or not bias.is_contiguous()):
+        raise RuntimeError("gemm_w4a4 bias must be contiguous fp16")
+    if workspace is None:
+        workspace = torch.empty((N * K,), dtype=torch.int8, device=a_q.device)
+    elif workspace.dtype != torch.int8 or workspace.numel() < N * K or not workspace.is_contiguous():
+        raise RuntimeError("gemm_w4a4 workspace must be contiguous int8 of at least N * K bytes")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=a_q.device)
+    call("b2_gemm_w4a4", ptr(a_q), ptr(w_packed), ptr(a_scale), ptr(w_scale), ptr(bias), ptr(out), I(M), I(N), I(K),
+         ptr(workspace), stream())
+    return out
+
+
 def attention(q, k, v, out, scale, int8_qk=False, workspace=None):
     """Fused attention on (B, H, L, 128) fp16 views with a contiguous last dimension; writes ``out``."""
     require_cuda(q, k, v, out)

@@ -66,6 +66,12 @@ int b2_quant_pack_a(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int
                     void* stream);
 int b2_quant_pack_a_seg(const uint16_t* x, int64_t ldx, int seg, int64_t seg_stride, int8_t* q, float* scale, int M,
                         int K, int rot_group, void* stream);
+/* Activations with int4 values for the per-channel W4A4 path (int8_gemm.hip:62-91 quant_row_i4, :266
+ * rot_quant_pack_a_i4; caller int8_gemm.py:90-103): after the rotation, scale = max(absmax, 1e-10) / 7 and
+ * q = clamp(rint(y / scale), -7, 7) (IEEE divide, half-even). q holds one int8 per value (the reference packs eight
+ * per dword for its dot8 instruction; the GEMM here reads bytes). rot_group 0, 128 or 256. */
+int b2_quant_pack_a_i4(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
+                       void* stream);
 /* h = fp16(fp16(silu(gate)) * up), as F.silu(gate).mul_(up) (int8_gemm.hip:129-132). */
 int b2_swiglu_quant_pack_a(const uint16_t* gate, const uint16_t* up, int64_t ld, int8_t* q, float* scale, int M,
                            int K, int rot_group, uint16_t* act_out, void* stream);
@@ -102,6 +108,18 @@ int b2_gemm_i32(const int8_t* A, const int8_t* B, int32_t* C32, int M, int N, in
  * Needs N % 256 == 0 and K % 16 == 0. */
 int b2_gemm_swiglu(const int8_t* A, const int8_t* B, const float* as, const float* ws, uint16_t* C, int M, int N,
                    int K, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Per-channel W4A4 GEMM, the reference's own int4 form (int8_gemm.hip:412 gemm_i4; int8_gemm.py:90-103):
+ *   acc = sum_k A[m, k] W[n, k] (int32, all of K); C = fp16((float)acc * as[m] * ws[n] (+ bias[n])), the W8A8
+ *   epilogue of b2_gemm. A: int8 [M, K] with values in [-7, 7] (b2_quant_pack_a_i4). Wp: packed uint8 [N, K/2],
+ *   low nibble = even k, two's-complement nibbles. ws: fp32 [N]. workspace: N * K bytes of device scratch
+ *   (16-byte aligned) that receives the widened weight, b2_unpack_int4 (as the reference re-packs its weight into a
+ *   per-call buffer, pack_b, int8_gemm.hip:270-276). K % 32 == 0, N % 8 == 0.
+ * ------------------------------------------------------------------------------------------------ */
+int b2_unpack_int4(const uint8_t* Wp, int8_t* W, int N, int K, void* stream);
+int b2_gemm_w4a4(const int8_t* A, const uint8_t* Wp, const float* as, const float* ws, const uint16_t* bias,
+                 uint16_t* C, int M, int N, int K, int8_t* workspace, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * W4A8 GEMM with group-128 weight scales (the configuration's tuned-int4 form). The reference's int4 path is

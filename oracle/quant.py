@@ -28,6 +28,18 @@ def quant_rows(y):
     return np.fmin(np.fmax(q, F32(-128)), F32(127)).astype(np.int8), scale
 
 
+def quant_rows_i4(y):
+    """Per-row int4-valued activations (int8_gemm.hip:62-91, quant_row_i4): scale = fmaxf(mx, 1e-10f) / 7.f (:71),
+    q = clamp(rintf(f / scale), -7, 7) (:85), i.e. round half to even after an IEEE divide; one int8 per value here
+    (the reference packs eight per dword, low nibble first, which only its dot8 instruction needs)."""
+    f = np.asarray(y).astype(F32)
+    mx = np.fmax.reduce(np.abs(f), axis=1, initial=F32(0)) if f.shape[1] else np.zeros(f.shape[0], F32)
+    scale = (np.maximum(mx, F32(1e-10)) / F32(7)).astype(F32)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = np.rint(f / scale[:, None])
+    return np.fmin(np.fmax(q, F32(-7)), F32(7)).astype(np.int8), scale
+
+
 def _h4(a, b, c, d):
     """One regular 4-point Hadamard step (int8_gemm.hip:106-109): s = ((a+b)+c)+d; (s-2d, s-2c, s-2b, s-2a)."""
     s = ((a + b) + c) + d

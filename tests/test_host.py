@@ -63,6 +63,11 @@ def test_validation_errors_before_any_launch(pkg):
     assert _status(pkg, "b2_gemv_i8_ex", fake, fake, fake, P(None), fake, fake, I(8), I(16), I(0), P(None)) == 1
     assert _status(pkg, "b2_decode_qk_rope", fake, fake, fake, fake, P(None), fake, fake, fake, I(8), I(2), F(1e-6),
                    P(None)) == 1
+    # int4 path: K % 32 for the unpack, a workspace for the W4A4 GEMM, rotation groups
+    assert _status(pkg, "b2_unpack_int4", fake, fake, I(8), I(48), P(None)) == 2
+    assert _status(pkg, "b2_gemm_w4a4", fake, fake, fake, fake, P(None), fake, I(4), I(8), I(64), P(None), P(None)) == 1
+    assert _status(pkg, "b2_gemm_w4a4", fake, fake, fake, fake, P(None), fake, I(4), I(12), I(64), fake, P(None)) == 2
+    assert _status(pkg, "b2_quant_pack_a_i4", fake, I64(512), fake, fake, I(4), I(512), I(64), P(None)) == 2
     # situ: the row stride must hold [hidden | gate]
     assert _status(pkg, "b2_situ_quant_pack_a", fake, I64(256), fake, fake, I(4), I(256), I(0), P(None), P(None)) == 1
     assert _status(pkg, "b2_situ_quant_pack_a", fake, I64(520), fake, fake, I(4), I(260), I(0), P(None), P(None)) == 2
@@ -107,6 +112,21 @@ def test_int8_linear_refuses_ineligible_inputs(pkg):
         f(torch.zeros((4, 64), dtype=torch.float16), w, 1.0, x_q=torch.zeros(1))
     with pytest.raises(NotImplementedError, match="fp16"):
         f(torch.zeros((4, 64)), w, 1.0)
+
+
+def test_w4a4_refuses_ineligible_inputs(pkg):
+    f = pkg.int8_gemm.wrap_w4a4(None)
+    x = torch.zeros((4, 512), dtype=torch.float16)
+    qw = torch.zeros((64, 256), dtype=torch.uint8)
+    ws = torch.ones(64)
+    with pytest.raises(NotImplementedError, match="ConvRot group 128"):
+        f(x, qw, ws, None, 128, torch.float16)
+    with pytest.raises(NotImplementedError, match="pre-rotated"):
+        f(x, qw, ws, None, 256, torch.float16, x_rot=x)
+    with pytest.raises(NotImplementedError, match="one per output channel"):
+        f(x, qw, torch.ones((64, 2)), None, 256, torch.float16)
+    with pytest.raises(NotImplementedError, match="fp16 compute"):
+        f(x, qw, ws, None, 256, torch.bfloat16)
 
 
 def _fake_packs():

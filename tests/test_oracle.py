@@ -97,6 +97,16 @@ def test_swiglu_and_gate_round_at_torch_points():
     assert np.mean(oq.sigmoid_gate(up, gate) != ref_g) < 1e-2
 
 
+def test_int4_activations_round_half_even():
+    # int8_gemm.hip:71,84: scale = max(mx, 1e-10) / 7; q = clamp(rint(f / scale), -7, 7); NaN -> -7.
+    row = np.array([[7, 3.5, 2.5, -2.5, 0.5, -0.5, 1.5, -6.5, np.nan]], dtype=F16)
+    q, s = oq.quant_rows_i4(row)
+    assert s[0] == 1.0
+    assert q.tolist() == [[7, 4, 2, -2, 0, 0, 2, -6, -7]]
+    q, s = oq.quant_rows_i4(np.zeros((1, 8), F16))
+    assert s[0] == np.float32(np.float32(1e-10) / np.float32(7)) and not q.any()
+
+
 def test_situ_is_soft_capped_gated_tanh():
     """int8_gemm.hip:118-127: situ(h, g) = 4 tanh(g/4) sigmoid(g) 25 tanh(h/25), tanh and sigmoid via 2^x with the
     odd series below |x| = 0.02; one fp16 rounding. Against float64 math: within one fp16 step; odd in h; bounded by

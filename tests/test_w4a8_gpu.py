@@ -67,3 +67,61 @@ def test_config3_linear(pkg, dev):
     assert np.array_equal(got, ref)
     exact = x.astype(np.float64) @ w.T.astype(np.float64)
     assert np.linalg.norm(got - exact) / np.linalg.norm(exact) < 0.15  # int4 weight error, for scale
+
+
+# ---------------------------------------------------------------- per-channel W4A4 (the reference's int4 form)
+@pytest.mark.parametrize("rot", [0, 128, 256])
+@pytest.mark.parametrize("M,K", [(1, 256), (77, 3072), (300, 1024)])
+def test_int4_activations_bit_exact(pkg, dev, rot, M, K):
+    """quant_row_i4 (int8_gemm.hip:62-91): scale = max(absmax, 1e-10) / 7, q = clamp(rint(y / scale), -7, 7)."""
+    g = np.random.default_rng(M + K + rot)
+    x = (g.standard_normal((M, K)) * 2).astype(F16)
+    q, s = pkg.ops.quant_pack_a_i4(dev_(x, dev), rot)
+    q_ref, s_ref = oq.quant_rows_i4(oq.rotate_rows(x, rot))
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
+def test_int4_activation_edges(pkg, dev):
+    """Half-way quotients round to even, a NaN becomes -7, an all-zero row takes the 1e-10 floor, inf rows."""
+    K = 256
+    x = np.zeros((5, K), F16)
+    x[0, :8] = [7, 3.5, 2.5, -2.5, 0.5, -0.5, 1.5, -6.5]   # scale 1: ties to even
+    x[1] = np.linspace(-1, 1, K).astype(F16)
+    x[1, 9] = np.nan
+    x[3] = np.linspace(-3, 3, K).astype(F16)
+    x[3, 4] = np.inf
+    x[4, 100] = -65504
+    for rot in (0, 256):
+        q, s = pkg.ops.quant_pack_a_i4(dev_(x, dev), rot)
+        q_ref, s_ref = oq.quant_rows_i4(oq.rotate_rows(x, rot))
+        assert np.array_equal(s.cpu().numpy(), s_ref), rot
+        assert np.array_equal(q.cpu().numpy(), q_ref), rot
+    q, _ = pkg.ops.quant_pack_a_i4(dev_(x, dev), 0)
+    assert q.cpu().numpy()[0, :8].tolist() == [7, 4, 2, -2, 0, 0, 2, -6]
+
+
+@pytest.mark.parametrize("N,K", [(8, 32), (264, 3072), (4096, 1024)])
+def test_unpack_int4_bit_exact(pkg, dev, N, K):
+    packed = np.random.default_rng(N + K).integers(0, 256, (N, K // 2), dtype=np.uint8)
+    got = pkg.ops.unpack_int4(dev_(packed, dev)).cpu().numpy()
+    assert np.array_equal(got, ogemm.unpack_int4(packed))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 8, 256), (130, 264, 1024), (2809, 3072, 3072)])
+def test_w4a4_convrot_forward_bit_exact(pkg, dev, M, N, K):
+    """convrot_w4a4_forward (int8_gemm.py:90-103): ConvRot-256 + int4-valued activations, packed int4 weights with
+    per-channel scales, int32 over all of K, the W8A8 epilogue; against the oracle bit for bit."""
+    g = np.random.default_rng(M + N)
+    x = g.standard_normal((M, K)).astype(F16)
+    packed = g.integers(0, 256, (N, K // 2), dtype=np.uint8)
+    ws = (g.random(N) * 1e-2 + 1e-4).astype(F32)
+    bias = (g.standard_normal(N) * 0.01).astype(F16)
+    fwd = pkg.int8_gemm.wrap_w4a4(None)
+    for b in (None, bias):
+        got = fwd(dev_(x, dev).view(1, M, K), dev_(packed, dev), dev_(ws, dev), None if b is None else dev_(b, dev), 256,
+                  torch.float16)
+        assert got.shape == (1, M, N)
+        q_ref, s_ref = oq.quant_rows_i4(oq.rotate_rows(x, 256))
+        ref = ogemm.epilogue(ogemm.int_mm(q_ref, ogemm.unpack_int4(packed)), s_ref, ws, b)
+        assert np.array_equal(got.cpu().numpy().reshape(M, N), ref)
