@@ -445,6 +445,77 @@ class W4A8C3:
         return 2.0 * M * N * K / dt / 1e12, "512 of the 2809 rows through the oracle pre-pass + per-group torch._int_mm + fp32 combine"
 
 
+class W4A4C3(W4A8C3):
+    """The reference's own int4 form on the C3 shapes: ConvRot-256 and int4-valued per-token activations, packed int4
+    weights with per-channel scales (int8_gemm.py:90-103); the packed weight is widened into a workspace and the
+    W8A8 GEMM accumulates in int32 over all of K."""
+    name = "w4a4"
+    metric = "W4A4 GEMM TOPS (C3 shapes 2809x3072x8192, int4 weights and activations, per-channel scales, pre-pass + widen + GEMM)"
+
+    def __init__(self, dev):
+        p = pkg()
+        self.ops = p.ops
+        g = np.random.default_rng(4)
+        x = g.standard_normal((self.M, self.K)).astype(np.float16)
+        self.x_host = torch.from_numpy(x).pin_memory()
+        packed = g.integers(0, 256, (self.N, self.K // 2), dtype=np.uint8)
+        per = self.M * self.K * 3 + self.N * self.K // 2 + self.M * self.N * 2
+        self.sets = max(2, math.ceil(2 * L2_BYTES / per))
+        self.xs = [self.x_host.to(dev) for _ in range(self.sets)]
+        self.ws = [torch.from_numpy(packed).to(dev) for _ in range(self.sets)]
+        self.wscale = torch.from_numpy((g.random(self.N) * 1e-2 + 1e-4).astype(np.float32)).to(dev)
+        self.workspace = torch.empty((self.N * self.K,), dtype=torch.int8, device=dev)
+        self.qs = [(torch.empty((self.M, self.K), dtype=torch.int8, device=dev),
+                    torch.empty((self.M,), dtype=torch.float32, device=dev)) for _ in range(self.sets)]
+        self.outs = [torch.empty((self.M, self.N), dtype=torch.float16, device=dev) for _ in range(self.sets)]
+        self.y_host = torch.empty((self.M, self.N), dtype=torch.float16).pin_memory()
+        self.events = []
+        self.launches_per_step = 3
+        self.ops_per_step = 2.0 * self.M * self.N * self.K
+        self.config = {"workload": "C3 shapes, per-channel W4A4", "M": self.M, "K": self.K, "N": self.N,
+                       "rotation": "ConvRot 256", "l2": "rotating input/weight sets > 2x L2"}
+
+    def step(self, i, record=False):
+        s = i % self.sets
+        q = self.ops.quant_pack_a_i4(self.xs[s], 256, out=self.qs[s])
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        self.ops.gemm_w4a4(q[0], q[1], self.ws[s], self.wscale, out=self.outs[s], workspace=self.workspace)
+        if record:
+            e1.record()
+            self.events.append((e0, e1))
+
+    def e2e_step(self, i):
+        s = i % self.sets
+        x = self.x_host.to(self.xs[s].device, non_blocking=True)
+        q = self.ops.quant_pack_a_i4(x, 256)
+        y = self.ops.gemm_w4a4(q[0], q[1], self.ws[s], self.wscale, workspace=self.workspace)
+        self.y_host.copy_(y, non_blocking=True)
+
+    def roofline(self, peaks, kms):
+        r = super().roofline(peaks, kms)
+        r.update(traffic=NCU_TRAFFIC.get("w4a4"), kernel="unpack_int4_kernel + gemm_w8a8_kernel (one timed pair)")
+        return r
+
+    @staticmethod
+    def cpu_baseline(threads):
+        from oracle import gemm as ogemm
+        from oracle import quant as oq
+
+        torch.set_num_threads(threads)
+        g = np.random.default_rng(4)
+        M, K, N = 512, W4A4C3.K, W4A4C3.N
+        x = g.standard_normal((M, K)).astype(np.float16)
+        packed = g.integers(0, 256, (N, K // 2), dtype=np.uint8)
+        ws = np.full(N, 1e-3, np.float32)
+        t0 = time.perf_counter()
+        q, s = oq.quant_rows_i4(oq.rotate_rows(x, 256))
+        ogemm.epilogue(ogemm.int_mm(q, ogemm.unpack_int4(packed)), s, ws)
+        dt = time.perf_counter() - t0
+        return 2.0 * M * N * K / dt / 1e12, "512 of the 2809 rows through the oracle ConvRot + int4 quant + torch._int_mm + epilogue"
+
+
 class GemmQKV(GemmC1):
     """The C4 QKV projection alone (M = 2 x 3321 tokens, N = 9216, K = 3072): the DiT step's GEMM shape."""
     name = "gemm_qkv"
@@ -871,7 +942,7 @@ class DiTC4:
 
 WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4,
              "w4a8": W4A8C3, "gemm_qkv": GemmQKV, "prepass": PrepassC4, "decode": DecodeC5,
-             "logits": LogitsC5}
+             "logits": LogitsC5, "w4a4": W4A4C3}
 
 
 def reference_arm(args, world, rank):
@@ -896,6 +967,10 @@ def reference_arm(args, world, rank):
         v, sample = DecodeC5.cpu_baseline(threads)
         metric, unit, higher = DecodeC5.metric, DecodeC5.unit, False
         cfg = {"workload": "C5 single-token decode", "layers": 36, "hidden": 2560, "kv_len": 1024}
+    elif name == "w4a4":
+        v, sample = W4A4C3.cpu_baseline(threads)
+        metric, unit, higher = W4A4C3.metric, W4A4C3.unit, True
+        cfg = {"workload": "C3 shapes, per-channel W4A4", "M": W4A4C3.M, "K": W4A4C3.K, "N": W4A4C3.N}
     elif name == "logits":
         v, sample = LogitsC5.cpu_baseline(threads)
         metric, unit, higher = LogitsC5.metric, LogitsC5.unit, True
