@@ -205,3 +205,28 @@ def test_decoder_fused_step_matches_torch_ops(pkg, dev):
     for lf, lr in zip(fused.layers, ref.layers):
         assert torch.allclose(lf.k_cache, lr.k_cache, rtol=1e-5, atol=1e-6)
         assert torch.equal(lf.v_cache, lr.v_cache) or torch.allclose(lf.v_cache, lr.v_cache, rtol=1e-5, atol=1e-6)
+
+
+def test_decoder_graph_replay_matches_eager(pkg, dev):
+    """The decode kernels launch with programmatic dependent launch, which a CUDA graph records as programmatic edges:
+    a captured step replayed must give the eager step's hidden state and caches bit for bit."""
+    import importlib
+
+    decoder = importlib.import_module(pkg.__name__ + ".decoder")
+    cfg = decoder.DecoderConfig(hidden=512, layers=3, heads=8, kv_heads=2, head_dim=128, mlp=1024, capacity=64)
+    eager, graphed = decoder.TextDecoder(cfg, dev, seed=2), decoder.TextDecoder(cfg, dev, seed=2)
+    x0 = torch.randn((1, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(6), device=dev)
+    for dec in (eager, graphed):
+        dec.x.copy_(x0)
+        dec.set_position(20)
+    eager.step_eager()
+    graphed.capture()  # runs the step once (position 20) before recording it
+    for pos in (21, 22):
+        eager.set_position(pos)
+        eager.step_eager()
+        graphed.set_position(pos)
+        graphed.step()
+    torch.cuda.synchronize()
+    assert torch.equal(eager.x, graphed.x)
+    for le, lg in zip(eager.layers, graphed.layers):
+        assert torch.equal(le.k_cache, lg.k_cache) and torch.equal(le.v_cache, lg.v_cache)
