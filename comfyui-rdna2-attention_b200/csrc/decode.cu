@@ -8,14 +8,6 @@
 // The GEMV streams the int8 weight once from HBM with 16-byte non-allocating loads, several rows and
 // several steps in flight per warp. int8 -> fp32 goes through a byte permute into the mantissa of
 // 2^23 (exact), which keeps the conversion off the narrow conversion pipe.
-//
-// A decode step is a chain of short kernels (9 per layer), so every kernel here is launched with programmatic
-// dependent launch: each waits (griddepcontrol.wait) until its predecessor on the stream has completed with its
-// memory visible, then lets its own successor launch, so the successor's launch and prologue overlap this kernel's
-// run. The int8 GEMV issues its first weight loads, and L2 prefetches of the rest of its rows, before its wait: the
-// weight stream of one GEMV overlaps the tail of the previous kernel. Only the immediate predecessor can still be
-// running at that point (it released this kernel after its own wait), so a GEMV's weight must not be written by the
-// kernel launched just before it.
 #include "common.cuh"
 #include "host.hpp"
 
@@ -28,8 +20,6 @@ constexpr int HEAD = 128;
 // ---------------------------------------------------------------- rotate
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, float* __restrict__ out, int group) {
     extern __shared__ float s[];
-    griddep_wait();
-    griddep_launch_dependents();
     const float* in = x + (int64_t)blockIdx.x * group;
     for (int i = threadIdx.x; i < group; i += 256) s[i] = in[i];
     __syncthreads();
@@ -77,8 +67,6 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
     return v;
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
-
 constexpr int GEMV_WARPS = 8;
 constexpr int GEMV_ROWS = 2;     // rows per warp
 constexpr int GEMV_UNROLL = 4;   // 512-value steps in flight per row
@@ -92,61 +80,42 @@ __device__ __forceinline__ float silu_mul_f32(float g, float u) {
 
 // act 1: x holds [gate | up] (2K values) and the GEMV input is silu(gate) * up, formed while x is staged.
 // residual: out[n] = residual[n] + y[n].
-__global__ void __launch_bounds__(GEMV_WARPS * 32, 4) gemv_i8_kernel(const float* __restrict__ x, const int8_t* __restrict__ w,
+__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_i8_kernel(const float* __restrict__ x, const int8_t* __restrict__ w,
                                                                  const float* __restrict__ scale,
                                                                  const float* __restrict__ bias,
                                                                  const float* __restrict__ residual, float* __restrict__ out,
                                                                  int N, int K, int act) {
     extern __shared__ float4 xs[];
     const int steps = (K + 511) / 512;
+    for (int i = threadIdx.x; i < steps * 128; i += blockDim.x) {
+        const int s = i >> 7, r = i & 127, l = r >> 2, j = r & 3;
+        const int k = i * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < K) {
+            v = *reinterpret_cast<const float4*>(x + k);
+            if (act) {
+                const float4 u = *reinterpret_cast<const float4*>(x + K + k);
+                v = make_float4(silu_mul_f32(v.x, u.x), silu_mul_f32(v.y, u.y), silu_mul_f32(v.z, u.z), silu_mul_f32(v.w, u.w));
+            }
+        }
+        xs[(s * 4 + j) * 32 + l] = v;
+    }
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS;
+    if (row0 >= N) return;
+    float acc[GEMV_ROWS] = {};
     const int8_t* wr[GEMV_ROWS];
 #pragma unroll
     for (int r = 0; r < GEMV_ROWS; ++r) wr[r] = w + (int64_t)min(row0 + r, N - 1) * K + lane * 16;
     const bool full_steps = (K % 512) == 0;
-    // Weights are read-only: the loop's first batch of loads and L2 prefetches of the rest of the rows go out before
-    // waiting for the kernel that produces x.
-    uint4 v[GEMV_UNROLL][GEMV_ROWS];
-    const bool pre = GEMV_UNROLL <= steps && (full_steps || GEMV_UNROLL < steps);  // the main loop runs
-    if (row0 < N) {
-        if (pre) {
-#pragma unroll
-            for (int u = 0; u < GEMV_UNROLL; ++u)
-#pragma unroll
-                for (int r = 0; r < GEMV_ROWS; ++r) v[u][r] = ld_stream(wr[r] + u * 512);
-        }
-        if ((lane & 7) == 0)  // one lane per 128-byte line
-            for (int st = pre ? GEMV_UNROLL : 0; st < steps && st * 512 + lane * 16 < K; ++st)
-#pragma unroll
-                for (int r = 0; r < GEMV_ROWS; ++r) prefetch_l2(wr[r] + st * 512);
-    }
-    griddep_wait();
-    griddep_launch_dependents();
-    for (int i = threadIdx.x; i < steps * 128; i += blockDim.x) {
-        const int s = i >> 7, r = i & 127, l = r >> 2, j = r & 3;
-        const int k = i * 4;
-        float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (k < K) {
-            xv = *reinterpret_cast<const float4*>(x + k);
-            if (act) {
-                const float4 u = *reinterpret_cast<const float4*>(x + K + k);
-                xv = make_float4(silu_mul_f32(xv.x, u.x), silu_mul_f32(xv.y, u.y), silu_mul_f32(xv.z, u.z), silu_mul_f32(xv.w, u.w));
-            }
-        }
-        xs[(s * 4 + j) * 32 + l] = xv;
-    }
-    __syncthreads();
-    if (row0 >= N) return;
-    float acc[GEMV_ROWS] = {};
     int s = 0;
     for (; s + GEMV_UNROLL <= steps && (full_steps || s + GEMV_UNROLL < steps); s += GEMV_UNROLL) {
-        if (s > 0) {  // the first batch was loaded before the wait
+        uint4 v[GEMV_UNROLL][GEMV_ROWS];
 #pragma unroll
-            for (int u = 0; u < GEMV_UNROLL; ++u)
+        for (int u = 0; u < GEMV_UNROLL; ++u)
 #pragma unroll
-                for (int r = 0; r < GEMV_ROWS; ++r) v[u][r] = ld_stream(wr[r] + (s + u) * 512);
-        }
+            for (int r = 0; r < GEMV_ROWS; ++r) v[u][r] = ld_stream(wr[r] + (s + u) * 512);
 #pragma unroll
         for (int u = 0; u < GEMV_UNROLL; ++u) {
             float4 xv[4];
@@ -201,25 +170,21 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_bf16_kernel(const float*
                                                                    const uint16_t* __restrict__ w,
                                                                    float* __restrict__ out, int N, int K) {
     extern __shared__ float4 xs[];
-    // One launch per token, at the end of the step: it only waits for its predecessor (the table is far larger than
-    // L2, so it is streamed once, after the wait).
-    griddep_wait();
-    griddep_launch_dependents();
     const int steps = (K + 255) / 256;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS;
-    const uint16_t* wr[GEMV_ROWS];
-#pragma unroll
-    for (int r = 0; r < GEMV_ROWS; ++r) wr[r] = w + (int64_t)min(row0 + r, N - 1) * K + lane * 8;
-    const bool full_steps = (K % 256) == 0;
     for (int i = threadIdx.x; i < steps * 64; i += blockDim.x) {
         const int s = i >> 6, r = i & 63, l = r >> 1, j = r & 1;
         const int k = i * 4;
         xs[(s * 2 + j) * 32 + l] = k < K ? *reinterpret_cast<const float4*>(x + k) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * GEMV_WARPS + warp) * GEMV_ROWS;
     if (row0 >= N) return;
     float acc[GEMV_ROWS] = {};
+    const uint16_t* wr[GEMV_ROWS];
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r) wr[r] = w + (int64_t)min(row0 + r, N - 1) * K + lane * 8;
+    const bool full_steps = (K % 256) == 0;
     int s = 0;
     for (; s + GEMV_UNROLL <= steps && (full_steps || s + GEMV_UNROLL < steps); s += GEMV_UNROLL) {
         uint4 v[GEMV_UNROLL][GEMV_ROWS];
@@ -267,8 +232,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(1024) rms_norm_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                            float* __restrict__ y, int D, float eps) {
     __shared__ float red[32];
-    griddep_wait();
-    griddep_launch_dependents();
     float ss = 0.f;
     for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
     ss = block_sum(ss, red);
@@ -288,8 +251,6 @@ __global__ void __launch_bounds__(HEAD) decode_qk_rope_kernel(const float* __res
                                                              int heads, int kv_heads, float eps) {
     __shared__ float red[4];
     __shared__ float ys[HEAD];
-    griddep_wait();
-    griddep_launch_dependents();
     const int hd = blockIdx.x, t = threadIdx.x;
     const int64_t p = *pos;
     const float x = qkv[(int64_t)hd * HEAD + t];
@@ -324,8 +285,6 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const float
                                                                     int capacity, int kv_heads, float scale) {
     __shared__ float4 acc_s[DEC_WARPS][GROUP][HEAD / 4];
     __shared__ float max_s[DEC_WARPS][GROUP], sum_s[DEC_WARPS][GROUP];
-    griddep_wait();
-    griddep_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.y / kv_heads, kvh = blockIdx.y % kv_heads, split = blockIdx.x;
     const int length = min(lengths[b], capacity);
@@ -394,8 +353,6 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) attn_decode_kernel(const float
 
 __global__ void __launch_bounds__(HEAD) attn_merge_kernel(const float* __restrict__ partial, const float* __restrict__ stats,
                                                          float* __restrict__ out) {
-    griddep_wait();
-    griddep_launch_dependents();
     const int64_t head = blockIdx.x;
     const float* st = stats + head * DEC_SPLITS * 2;
     float top = st[0];
@@ -407,24 +364,6 @@ __global__ void __launch_bounds__(HEAD) attn_merge_kernel(const float* __restric
         total += st[s * 2 + 1] * keep;
     }
     out[head * HEAD + threadIdx.x] = value / total;
-}
-
-// Split-KV decode attention and its merge, both launched with programmatic dependent launch.
-int launch_attn_decode(int group, dim3 grid, cudaStream_t s, const float* q, const float* k, const float* v,
-                       const int32_t* lengths, float* partial, float* stats, float* out, int rows, int capacity,
-                       int kv_heads, float scale) {
-    int rc;
-    const dim3 block(DEC_WARPS * 32);
-    switch (group) {
-        case 1: rc = launch_pdl("attn_decode_kernel", attn_decode_kernel<1>, grid, block, 0, s, q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 2: rc = launch_pdl("attn_decode_kernel", attn_decode_kernel<2>, grid, block, 0, s, q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 4: rc = launch_pdl("attn_decode_kernel", attn_decode_kernel<4>, grid, block, 0, s, q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 8: rc = launch_pdl("attn_decode_kernel", attn_decode_kernel<8>, grid, block, 0, s, q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        default: return fail(B2_ERR_UNSUPPORTED, "attn_decode: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
-    }
-    if (rc) return rc;
-    return launch_pdl("attn_merge_kernel", attn_merge_kernel, dim3(rows), dim3(HEAD), 0, s, (const float*)partial,
-                      (const float*)stats, out);
 }
 
 }  // namespace
@@ -441,8 +380,8 @@ extern "C" int b2_rotate(const float* x, float* out, int64_t n, int group, void*
     const int smem = group * 4;
     if (smem > 48 * 1024)
         if (int rc = set_smem(rotate_kernel, smem)) return rc;
-    return launch_pdl("rotate_kernel", rotate_kernel, dim3((unsigned)(n / group)), dim3(256), smem, (cudaStream_t)stream, x,
-                      out, group);
+    rotate_kernel<<<(unsigned)(n / group), 256, smem, (cudaStream_t)stream>>>(x, out, group);
+    return check_launch("rotate_kernel");
 }
 
 extern "C" int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
@@ -457,8 +396,9 @@ extern "C" int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, c
     if (smem > 48 * 1024)
         if (int rc = set_smem(gemv_i8_kernel, smem)) return rc;
     const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
-    return launch_pdl("gemv_i8_kernel", gemv_i8_kernel, dim3((N + rows_per_cta - 1) / rows_per_cta), dim3(GEMV_WARPS * 32),
-                      smem, (cudaStream_t)stream, x, w, scale, bias, (const float*)nullptr, out, N, K, 0);
+    gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(
+        x, w, scale, bias, nullptr, out, N, K, 0);
+    return check_launch("gemv_i8_kernel");
 }
 
 extern "C" int b2_gemv_i8_ex(const float* x, const int8_t* w, const float* scale, const float* bias, const float* residual,
@@ -475,8 +415,9 @@ extern "C" int b2_gemv_i8_ex(const float* x, const int8_t* w, const float* scale
     if (smem > 48 * 1024)
         if (int rc = set_smem(gemv_i8_kernel, smem)) return rc;
     const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
-    return launch_pdl("gemv_i8_kernel", gemv_i8_kernel, dim3((N + rows_per_cta - 1) / rows_per_cta), dim3(GEMV_WARPS * 32),
-                      smem, (cudaStream_t)stream, x, w, scale, bias, residual, out, N, K, act);
+    gemv_i8_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(
+        x, w, scale, bias, residual, out, N, K, act);
+    return check_launch("gemv_i8_kernel");
 }
 
 extern "C" int b2_gemv_bf16(const float* x, const uint16_t* w, float* out, int N, int K, void* stream) {
@@ -490,14 +431,15 @@ extern "C" int b2_gemv_bf16(const float* x, const uint16_t* w, float* out, int N
     if (smem > 48 * 1024)
         if (int rc = set_smem(gemv_bf16_kernel, smem)) return rc;
     const int rows_per_cta = GEMV_WARPS * GEMV_ROWS;
-    return launch_pdl("gemv_bf16_kernel", gemv_bf16_kernel, dim3((N + rows_per_cta - 1) / rows_per_cta),
-                      dim3(GEMV_WARPS * 32), smem, (cudaStream_t)stream, x, w, out, N, K);
+    gemv_bf16_kernel<<<(N + rows_per_cta - 1) / rows_per_cta, GEMV_WARPS * 32, smem, (cudaStream_t)stream>>>(x, w, out, N,
+                                                                                                            K);
+    return check_launch("gemv_bf16_kernel");
 }
 
 extern "C" int b2_rms_norm_f32(const float* x, const float* w, float* y, int D, float eps, void* stream) {
     if (!x || !w || !y || D <= 0) return fail(B2_ERR_INVALID, "rms_norm_f32: bad arguments");
-    return launch_pdl("rms_norm_f32_kernel", rms_norm_f32_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, x, w, y, D,
-                      eps);
+    rms_norm_f32_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, w, y, D, eps);
+    return check_launch("rms_norm_f32_kernel");
 }
 
 extern "C" int b2_decode_qk_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* inv_freq,
@@ -505,9 +447,9 @@ extern "C" int b2_decode_qk_rope(const float* qkv, const float* q_norm, const fl
                                  int kv_heads, float eps, void* stream) {
     if (!qkv || !q_norm || !k_norm || !inv_freq || !pos || !q_out || !k_cache || !v_cache || heads <= 0 || kv_heads <= 0)
         return fail(B2_ERR_INVALID, "decode_qk_rope: bad arguments");
-    return launch_pdl("decode_qk_rope_kernel", decode_qk_rope_kernel, dim3(heads + 2 * kv_heads), dim3(HEAD), 0,
-                      (cudaStream_t)stream, qkv, q_norm, k_norm, inv_freq, pos, q_out, k_cache, v_cache, heads, kv_heads,
-                      eps);
+    decode_qk_rope_kernel<<<heads + 2 * kv_heads, HEAD, 0, (cudaStream_t)stream>>>(qkv, q_norm, k_norm, inv_freq, pos, q_out,
+                                                                                   k_cache, v_cache, heads, kv_heads, eps);
+    return check_launch("decode_qk_rope_kernel");
 }
 
 extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out,
@@ -518,8 +460,18 @@ extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, co
         return fail(B2_ERR_INVALID, "attn_decode: bad shape");
     const int group = heads / kv_heads;
     if (batch == 0) return B2_OK;
-    return launch_attn_decode(group, dim3(DEC_SPLITS, batch * kv_heads), (cudaStream_t)stream, q, k, v, lengths, partial,
-                              stats, out, batch * heads, capacity, kv_heads, scale);
+    dim3 grid(DEC_SPLITS, batch * kv_heads);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (group) {
+        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 8: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        default: return fail(B2_ERR_UNSUPPORTED, "attn_decode: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
+    }
+    if (int rc = check_launch("attn_decode_kernel")) return rc;
+    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
+    return check_launch("attn_merge_kernel");
 }
 
 // ---------------------------------------------------------------- decode attention without allocation
@@ -580,6 +532,15 @@ extern "C" int b2_attn_decode_noalloc(const float* q, const float* k, const floa
     // contents never leak into a result and nothing needs clearing.
     float* partial = scratch;
     float* stats = scratch + NOALLOC_PARTIAL;
-    return launch_attn_decode(group, dim3(DEC_SPLITS, batch * kv_heads), (cudaStream_t)stream, q, k, v, lengths, partial,
-                              stats, out, batch * heads, capacity, kv_heads, scale);
+    dim3 grid(DEC_SPLITS, batch * kv_heads);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (group) {
+        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        default: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+    }
+    if (int rc = check_launch("attn_decode_kernel(noalloc)")) return rc;
+    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
+    return check_launch("attn_merge_kernel(noalloc)");
 }

@@ -38,32 +38,6 @@ int make_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, i
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Launches a kernel with programmatic dependent launch allowed: it may start while the previous kernel on the
-// stream is still running, and must execute griddepcontrol.wait before it reads anything a previous kernel wrote or
-// writes anything a previous kernel may still read. Kernels launched this way call griddep_wait() before any such
-// access; their loads of read-only data (weights) may come first and overlap the previous kernel's tail. Inside a
-// stream capture the launch becomes a programmatic edge of the graph.
-template <typename... KArgs, typename... Args>
-inline int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                      cudaStream_t stream, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        return fail(B2_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-    }
-    return check_launch(what);
-}
-
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

@@ -167,11 +167,7 @@ int b2_rms_norm_rope(const uint16_t* x, const float* w, uint16_t* y, int rows, i
  * (int8_gemv.hip:108-129 rotate; int8_gemv.py:42-45). n % group == 0. */
 int b2_rotate(const float* x, float* out, int64_t n, int group, void* stream);
 /* out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32 (int8_gemv.hip:131-162 gemv_i8;
- * int8_gemv.py:62-63). K % 16 == 0.
- * The decode entry points below (rotate, GEMVs, RMSNorm, q/k rope, decode attention) launch with programmatic
- * dependent launch: each kernel waits for the previous kernel on the stream before it reads activations or writes
- * anything, and lets the next one launch early. The int8 GEMVs read their weight w before that wait, so w must not
- * be written by the kernel launched immediately before them on the same stream (weights are normally resident). */
+ * int8_gemv.py:62-63). K % 16 == 0. */
 int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
                void* stream);
 /* out[n] = sum_k w[n,k] x[k] in fp32 for a bf16 table w [N, K] (int8_gemv.hip:87-119 gemv_bf16; the logits of

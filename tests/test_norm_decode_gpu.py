@@ -208,8 +208,8 @@ def test_decoder_fused_step_matches_torch_ops(pkg, dev):
 
 
 def test_decoder_graph_replay_matches_eager(pkg, dev):
-    """The decode kernels launch with programmatic dependent launch, which a CUDA graph records as programmatic edges:
-    a captured step replayed must give the eager step's hidden state and caches bit for bit."""
+    """A captured decode step replayed from its CUDA graph (position and cache length read on the device) gives the
+    eager step's hidden state and caches bit for bit, token after token."""
     import importlib
 
     decoder = importlib.import_module(pkg.__name__ + ".decoder")
