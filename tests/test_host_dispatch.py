@@ -1,0 +1,181 @@
+"""Host-side dispatch without a GPU: the drop-in modules and drivers run on CPU tensors with the C-ABI call replaced
+by a recorder, so every tensor they hand to the library passes the wrappers' size/dtype checks and the sequence of
+entry points is the documented one (the DiT block's 9 launches, the decode layer's 9, the Krea-2 fused block's
+side-channel hand-offs, the W4A4 and situ paths). The numerics of the same paths are the GPU tests' job."""
+import types
+
+import pytest
+import torch
+
+
+@pytest.fixture
+def calls(pkg, monkeypatch):
+    log = []
+    monkeypatch.setattr(pkg.ops, "call", lambda name, *args: log.append(name))
+    monkeypatch.setattr(pkg.ops, "require_cuda", lambda *tensors: None)
+    monkeypatch.setattr(pkg.ops, "stream", lambda: None)
+    return log
+
+
+def test_dit_block_is_nine_launches(pkg, calls):
+    import importlib
+
+    dit = importlib.import_module(pkg.__name__ + ".dit")
+    cfg = dit.DiTConfig(hidden=256, heads=2, mlp=512, blocks=2, batch=2, tokens=40)
+    stack = dit.DiTStack(cfg, dit.shard_plan(1, 0, cfg.batch, cfg.heads), "cpu")
+    stack.forward(torch.randn((2, 40, 256)).half())
+    block = ["b2_mod_quant_pack_a", "b2_gemm", "b2_attention", "b2_quant_pack_a", "b2_gemm", "b2_mod_quant_pack_a",
+             "b2_gemm_swiglu", "b2_quant_pack_a", "b2_gemm"]
+    assert calls == block * cfg.blocks
+
+
+def test_dit_head_group_reads_the_gathered_segments(pkg, calls):
+    import importlib
+
+    dit = importlib.import_module(pkg.__name__ + ".dit")
+    cfg = dit.DiTConfig(hidden=256, heads=2, mlp=512, blocks=1, batch=2, tokens=40)
+    plan = dit.shard_plan(4, 1, cfg.batch, cfg.heads)
+    gathered = []
+    stack = dit.DiTStack(cfg, plan, "cpu", all_gather=lambda out, inp: gathered.append((out.numel(), inp.numel())))
+    stack.forward(torch.randn((1, 40, 256)).half())
+    assert "b2_quant_pack_a_seg" in calls and gathered == [(40 * 256, 40 * 128)]
+
+
+def test_decoder_layer_is_nine_launches(pkg, calls):
+    import importlib
+
+    decoder = importlib.import_module(pkg.__name__ + ".decoder")
+    cfg = decoder.DecoderConfig(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=128, mlp=512, capacity=16)
+    dec = decoder.TextDecoder(cfg, "cpu")
+    dec.set_position(3)
+    dec.step_eager()
+    layer = ["b2_rms_norm_f32", "b2_gemv_i8", "b2_decode_qk_rope", "b2_attn_decode", "b2_gemv_i8_ex",
+             "b2_rms_norm_f32", "b2_gemv_i8", "b2_gemv_i8_ex"]
+    assert calls == layer * cfg.layers
+    assert decoder.TextDecoder.launches_per_layer == len(layer) + 1  # attn_decode is two kernels (split, merge)
+
+
+def _linear(pkg, N, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    s = torch.rand(N, generator=g) * 1e-3
+    f = pkg.int8_gemm.wrap(None)
+
+    def forward(x):
+        # What the Int8 loader's Linear does: ConvRot hand-off, then the patched triton_int8_linear.
+        return f(pkg.int8_gemm.rotate_activation(x, None, 256), w, s)
+    return types.SimpleNamespace(__call__=forward, forward=forward, in_features=K)
+
+
+class _Call:
+    def __init__(self, fn):
+        self.fn = fn
+
+    def __call__(self, x):
+        return self.fn(x)
+
+
+def test_krea2_block_forward_hand_offs(pkg, calls):
+    """int8_gemm.block_forward (int8_gemm.py:189-226): the modulated norm quantized once for wq/wk/wv/gate, QK-norm +
+    rope, attention, the sigmoid gate in the out-projection's pre-pass with the gated residual, the second norm for
+    gate/up, the SwiGLU in the down projection's pre-pass with the gated residual."""
+    gm = pkg.int8_gemm
+    B, L, D, H = 1, 24, 256, 2
+    mk = lambda n, k, s: _Call(_linear(pkg, n, k, s).forward)  # noqa: E731
+    norm = lambda: types.SimpleNamespace(scale=torch.randn(D) * 0.02, eps=1e-6)  # noqa: E731
+    qk = types.SimpleNamespace(qnorm=types.SimpleNamespace(scale=torch.zeros(128), eps=1e-6),
+                               knorm=types.SimpleNamespace(scale=torch.zeros(128), eps=1e-6))
+    attn = types.SimpleNamespace(wq=mk(D, D, 1), wk=mk(D, D, 2), wv=mk(D, D, 3), gate=mk(D, D, 4), wo=mk(D, D, 5),
+                                 heads=H, kvheads=H, headdim=128, qknorm=qk)
+    mlp = types.SimpleNamespace(gate=mk(512, D, 6), up=mk(512, D, 7), down=mk(D, 512, 8))
+    mods = [torch.randn((B, 1, D)).half() * 0.1 for _ in range(6)]
+    module = types.SimpleNamespace(attn=attn, mlp=mlp, mod=lambda vec: mods, prenorm=norm(), postnorm=norm())
+    freqs = torch.randn((1, 1, L, 64, 2, 2))
+    out = gm.block_forward(module, False, torch.randn((B, L, D)).half(), None, freqs)
+    assert out.shape == (B, L, D)
+    assert calls == ["b2_mod_quant_pack_a", "b2_gemm", "b2_gemm", "b2_gemm", "b2_gemm", "b2_rms_norm_rope",
+                     "b2_rms_norm_rope", "b2_attention", "b2_gate_quant_pack_a", "b2_gemm", "b2_mod_quant_pack_a",
+                     "b2_gemm", "b2_gemm", "b2_swiglu_quant_pack_a", "b2_gemm"]
+    assert gm.shared is None and gm.swiglu_up is None and gm.sigmoid_gate is None and gm.residual is None
+
+
+def test_drop_in_entry_points_dispatch(pkg, calls):
+    # attention_hip: (B, L, H*D) and (B, H, L, D) with skip_reshape
+    q = torch.randn((2, 30, 2 * 128)).half()
+    assert pkg.attention.attention_hip(q, q, q, 2).shape == q.shape
+    qh = q.view(2, 30, 2, 128).transpose(1, 2)
+    assert pkg.attention.attention_hip(qh, qh, qh, 2, skip_reshape=True, skip_output_reshape=True).shape == qh.shape
+    # rms_norm drop-ins
+    m = types.SimpleNamespace(scale=torch.zeros(256), eps=1e-6)
+    pkg.rms_norm.forward(m, torch.randn((2, 5, 256)).half())
+    mh = types.SimpleNamespace(scale=torch.zeros(128), eps=1e-6)
+    pkg.rms_norm.rms_norm_rope(torch.randn((2, 7, 2 * 128)).half(), 2, mh, torch.randn((2, 1, 7, 64, 2, 2)))
+    # int8 linears: plain, rotated, situ, SwiGLU and gate flavours of the pre-pass
+    g = pkg.int8_gemm
+    w, s = torch.randint(-127, 128, (64, 256), dtype=torch.int8), torch.rand(64)
+    x = torch.randn((9, 256)).half()
+    g.linear(x, w, s, None)
+    g.linear(x, w, s, None, rotate=True)
+    g.linear(torch.randn((9, 512)).half(), w, s, None, situ=True)
+    g.linear(x, w, s, None, rotate=True, up=x.clone())
+    g.linear(x, w, s, None, gate=x.clone())
+    # per-channel W4A4
+    g.wrap_w4a4(None)(torch.randn((3, 5, 512)).half(), torch.zeros((64, 256), dtype=torch.uint8), torch.ones(64), None,
+                      256, torch.float16)
+    # decode: GEMV with and without ConvRot, logits, decode attention
+    gv = pkg.int8_gemv
+    lin = types.SimpleNamespace(weight=types.SimpleNamespace(_qdata=torch.zeros((32, 256), dtype=torch.int8),
+                                                             _params=types.SimpleNamespace(scale=torch.ones(32))),
+                                bias=None, weight_function=[], bias_function=[])
+    gv.linear_forward(lin, 32, 256, torch.int8, 0, torch.randn((1, 1, 256)))
+    gv.linear_forward(lin, 32, 256, torch.int8, 256, torch.randn((1, 1, 256)))
+    embed = types.SimpleNamespace(weight=torch.zeros((48, 256), dtype=torch.bfloat16), weight_function=[],
+                                  bias_function=[])
+    assert gv.logits(types.SimpleNamespace(model=types.SimpleNamespace(embed_tokens=embed)),
+                     torch.randn((1, 4, 256))).shape == (1, 1, 48)
+    gv.attention_decode(torch.randn((1, 1, 8, 128)), torch.randn((1, 16, 2, 128)), torch.randn((1, 16, 2, 128)),
+                        torch.tensor([5], dtype=torch.int32))
+    assert calls == ["b2_attention", "b2_attention", "b2_rms_norm", "b2_rms_norm_rope",
+                     "b2_quant_pack_a", "b2_gemm", "b2_quant_pack_a", "b2_gemm", "b2_situ_quant_pack_a", "b2_gemm",
+                     "b2_swiglu_quant_pack_a", "b2_gemm", "b2_gate_quant_pack_a", "b2_gemm",
+                     "b2_quant_pack_a_i4", "b2_gemm_w4a4",
+                     "b2_gemv_i8", "b2_rotate", "b2_gemv_i8", "b2_gemv_bf16", "b2_attn_decode"]
+
+
+def test_wrappers_refuse_buffers_the_kernels_would_overrun(pkg, calls):
+    ops = pkg.ops
+    a, w = torch.zeros((8, 64), dtype=torch.int8), torch.zeros((16, 64), dtype=torch.int8)
+    with pytest.raises(RuntimeError, match="activation scale"):
+        ops.gemm(a, torch.ones(4), w, torch.ones(16))
+    with pytest.raises(RuntimeError, match="weight scale"):
+        ops.gemm(a, torch.ones(8), w, torch.ones(15))
+    with pytest.raises(RuntimeError, match="gemm output"):
+        ops.gemm(a, torch.ones(8), w, torch.ones(16), out=torch.empty((8, 8), dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="bias"):
+        ops.gemm(a, torch.ones(8), w, torch.ones(16), bias=torch.zeros(16))
+    with pytest.raises(RuntimeError, match="quantized output"):
+        ops.quant_pack_a(torch.zeros((4, 64)).half(), out=(torch.empty((4, 32), dtype=torch.int8), torch.empty(4)))
+    with pytest.raises(RuntimeError, match="act_out"):
+        ops.swiglu_quant_pack_a(torch.zeros((4, 64)).half(), torch.zeros((4, 64)).half(),
+                                act_out=torch.empty((4, 32)).half())
+    q = torch.zeros((2, 2, 8, 128)).half()
+    with pytest.raises(RuntimeError, match="k and v"):
+        ops.attention(q, torch.zeros((1, 2, 8, 128)).half(), torch.zeros((1, 2, 8, 128)).half(), q, 1.0)
+    with pytest.raises(RuntimeError, match="k and v"):
+        ops.attention(q, q, torch.zeros((2, 2, 9, 128)).half(), q, 1.0)
+    with pytest.raises(RuntimeError, match="gemv_i8 output"):
+        ops.gemv_i8(torch.zeros(64), w, torch.ones(16), out=torch.empty(8))
+    with pytest.raises(RuntimeError, match="gemv_i8 scale"):
+        ops.gemv_i8(torch.zeros(64), w, torch.ones(16, dtype=torch.float64))
+    with pytest.raises(RuntimeError, match="lengths"):
+        ops.attn_decode(torch.zeros((2, 1, 4, 128)), torch.zeros((2, 8, 2, 128)), torch.zeros((2, 8, 2, 128)),
+                        torch.zeros(2, dtype=torch.int64), 1.0)
+    with pytest.raises(RuntimeError, match="segments reach past"):
+        ops.quant_pack_a_segments(torch.zeros(4 * 10 * 128).half(), 512, 128, 128, 10 * 128, 11, 128)
+    with pytest.raises(RuntimeError, match="workspace"):
+        ops.gemm_w4a4(a, torch.ones(8), torch.zeros((16, 32), dtype=torch.uint8), torch.ones(16),
+                      workspace=torch.empty(10, dtype=torch.int8))
+    with pytest.raises(RuntimeError, match="rope frequencies"):
+        ops.rms_norm_rows(torch.zeros((2, 3, 128)).half(), torch.zeros(128), 1e-6, 6, 128, 3, 1, 384, 0, 128,
+                          torch.empty((2, 3, 128)).half(), freqs=torch.zeros((1, 1, 2, 64, 2, 2)))
+    assert calls == []
