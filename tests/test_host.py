@@ -172,6 +172,49 @@ def test_enable_installs_and_removes_patches(pkg):
         g.fusable = False
 
 
+def test_situ_hand_off_through_linear_input_act(pkg):
+    """int8_gemm.py:152-157: for a fusable situ layer, linear_input_act sets situ_next and calls the linear on the raw
+    [hidden | gate] input, whose int8_linear then runs the situ pre-pass; anything else goes to ComfyUI's own
+    linear_input_act. enable() installs it into comfy.ops and restores it."""
+    g = pkg.int8_gemm
+    pack, convrot = _fake_packs()
+    comfy = types.ModuleType("comfy")
+    comfy_ops = types.ModuleType("comfy.ops")
+    comfy_ops.linear_input_act = lambda *a, **k: "core"
+    comfy.ops = comfy_ops
+    mods = {"fakepack.int8_quant": pack, "fakepack.convrot": convrot, "comfy": comfy, "comfy.ops": comfy_ops}
+    saved = {k: sys.modules.get(k) for k in mods}
+    sys.modules.update(mods)
+    try:
+        g.originals.clear()
+        g.enable(True)
+        assert comfy_ops.linear_input_act is g.linear_input_act
+        layer = types.SimpleNamespace(_is_quantized=True, _use_convrot=True, _convrot_groupsize=256, lora_patches=[],
+                                      in_features=512)
+        seen = []
+
+        def linear(x):
+            seen.append(g.situ_next)
+            g.situ_next = False
+            return "fused"
+        x = torch.zeros((3, 1024), dtype=torch.float16)
+        fused = type("L", (), {"__call__": lambda self, t: linear(t), **vars(layer)})()
+        assert g.linear_input_act(fused, x, "situ") == "fused" and seen == [True]
+        assert g.linear_input_act(fused, x, "swiglu") == "core"
+        assert g.linear_input_act(fused, x.float(), "situ") == "core"
+        assert g.linear_input_act(fused, x, "situ", residual=torch.zeros(1)) == "core"
+        g.enable(False)
+        assert comfy_ops.linear_input_act() == "core"
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+        g.originals.clear()
+        g.situ_next = False
+
+
 def test_swiglu_interleave_pairs_gate_and_up_blocks(pkg):
     """Row i of the interleaved gate/up weight: block j = i // 256 holds gate rows [128 j, 128 j + 128) then the
     matching up rows [F + 128 j, F + 128 j + 128)."""
