@@ -179,3 +179,33 @@ def test_wrappers_refuse_buffers_the_kernels_would_overrun(pkg, calls):
         ops.rms_norm_rows(torch.zeros((2, 3, 128)).half(), torch.zeros(128), 1e-6, 6, 128, 3, 1, 384, 0, 128,
                           torch.empty((2, 3, 128)).half(), freqs=torch.zeros((1, 1, 2, 64, 2, 2)))
     assert calls == []
+
+
+def test_prefill_routes_while_generating(pkg, calls):
+    """While generating, a multi-token fp32 input of a linear with a ConvRot group above 256 runs the rotation kernel
+    and a dense fp32 linear on the dequantized weight (int8_gemv.py:49-57); a gated MLP runs one stacked gate|up
+    linear (:67-75). With a group of 256 or less the layer's own forward runs (no launch)."""
+    gv = pkg.int8_gemv
+    qdata = torch.randint(-127, 128, (32, 1024), dtype=torch.int8)
+
+    class Linear:
+        weight = types.SimpleNamespace(_qdata=qdata, _params=types.SimpleNamespace(scale=torch.rand(32)))
+        bias, weight_function, bias_function = None, [], []
+
+        def forward(self, x):
+            return "core"
+
+    lin = Linear()
+    x = torch.randn((1, 5, 1024))
+    gv.generating = True
+    try:
+        y = gv.linear_forward(lin, 32, 1024, torch.int8, 1024, x)
+        assert y.shape == (1, 5, 32) and calls == ["b2_rotate"]
+        assert gv.linear_forward(lin, 32, 1024, torch.int8, 256, x) == "core"
+        gate, up = Linear(), Linear()
+        mlp = types.SimpleNamespace(gate_proj=gate, up_proj=up, activation=torch.nn.functional.silu,
+                                    down_proj=lambda h: h)
+        h = gv.mlp_forward(mlp, torch.int8, x)
+        assert h.shape == (1, 5, 32) and calls == ["b2_rotate"]
+    finally:
+        gv.generating = False
