@@ -11,7 +11,8 @@ Differences, all by design of this build: every linear runs the sm_100a kernels 
 weight as stored: no pack_b), for any row count, so MIN_ROWS is 1; inputs the kernels cannot take raise instead of
 falling back to the pack's Triton path; the rotation group is a parameter (256 = ConvRot as in the reference, 128 =
 the block-128 configuration). ``wrap_w4a4`` runs the Int4 loader's per-channel W4A4 layers (int8_gemm.py:90-103) and
-``linear_input_act`` hands situ activations to the pre-pass (:152-157), as in the reference.
+``linear_input_act`` hands situ activations to the pre-pass (:152-157), as in the reference; ``w4a8_forward`` is the
+configuration-3 W4A8 (group-128 scales) in the same call shape.
 """
 import functools
 import logging
@@ -147,6 +148,27 @@ def wrap_w4a4(original):
         out = ops.gemm_w4a4(a_q, a_s, qweight.contiguous(), wscales.reshape(N).float().contiguous(), bias)
         return out.reshape(x.shape[:-1] + (N,))
     return convrot_w4a4_forward
+
+
+def w4a8_forward(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation=False,
+                 qweight_unpacked=None, x_rot=None, orig_shape=None):
+    """W4A8 with group-128 weight scales (the configuration-3 form) in the call shape of convrot_w4a4_forward
+    (int8_gemm.py:91): x fp16 (..., K) is rotated by ``convrot_groupsize`` (128: block-128 Sylvester, 256: ConvRot)
+    and quantized per token to int8 in one pre-pass; qweight is packed int4 [N, K/2] (low nibble = even k); wscales
+    are fp16 [N, K/128], one scale per output channel and 128 values of K. The GEMM combines the int32 partial sum of
+    each 128-value group with its scale in fp32, in group order, then scales by the token's scale (+ bias)."""
+    N, K = qweight.shape[0], qweight.shape[1] * 2
+    if x_rot is not None or skip_rotation:
+        raise NotImplementedError("w4a8_forward: a pre-rotated input (x_rot / skip_rotation)")
+    if convrot_groupsize not in (ROT_GROUP, 128) or compute_dtype != torch.float16 or x.shape[-1] != K or K % 128:
+        raise NotImplementedError(f"w4a8_forward: group {convrot_groupsize}, {compute_dtype}, K={K} (needs 128 or 256, "
+                                  "fp16, K % 128 == 0)")
+    if tuple(wscales.shape) != (N, K // 128):
+        raise NotImplementedError(f"w4a8_forward: scales of shape {tuple(wscales.shape)}, expected ({N}, {K // 128})")
+    x2d = x.reshape(-1, K).to(torch.float16).contiguous()
+    a_q, a_s = ops.quant_pack_a(x2d, convrot_groupsize)
+    out = ops.gemm_w4a8(a_q, a_s, qweight.contiguous(), ops.w4a8_scales(wscales.to(torch.float16)), bias)
+    return out.reshape(x.shape[:-1] + (N,))
 
 
 def rotate_activation(x, H, group_size):

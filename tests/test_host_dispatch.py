@@ -209,3 +209,13 @@ def test_prefill_routes_while_generating(pkg, calls):
         assert h.shape == (1, 5, 32) and calls == ["b2_rotate"]
     finally:
         gv.generating = False
+
+
+def test_w4a8_forward_dispatch(pkg, calls):
+    """int8_gemm.w4a8_forward: block-128 rotation + int8 pre-pass, then the group-128 W4A8 GEMM."""
+    f = pkg.int8_gemm.w4a8_forward
+    x = torch.randn((2, 7, 512)).half()
+    out = f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones((64, 4)).half(), None, 128, torch.float16)
+    assert out.shape == (2, 7, 64) and calls == ["b2_quant_pack_a", "b2_gemm_w4a8"]
+    with pytest.raises(NotImplementedError, match="scales of shape"):
+        f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones(64).half(), None, 128, torch.float16)
