@@ -1,6 +1,7 @@
 """Generates tests/golden/attention_bmm.npz from the reference's own ``attention_bmm`` (attention.py:15-43).
 
-Runs only where the reference checkout is present (REF_DIR, default /root/reference). The reference package imports
+Runs only where the reference checkout is present: the environment variable REF_DIR names its directory. The
+reference package imports
 ComfyUI and a HIP loader at module level, which do not exist here, so this script loads ``attention.py`` alone as a
 submodule of a bare package object and stubs exactly the two names it imports: ``comfy.ldm.modules.attention
 .attention_pytorch`` (only reached with a mask) and the sibling ``hip_attention`` module (only reached by
@@ -14,7 +15,7 @@ import types
 import numpy as np
 import torch
 
-REF_DIR = os.environ.get("REF_DIR", "/root/reference")
+REF_DIR = os.environ.get("REF_DIR", "")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "attention_bmm.npz")
 
 
@@ -32,6 +33,8 @@ def load_reference_attention():
 
 
 def main():
+    if not REF_DIR or not os.path.isfile(os.path.join(REF_DIR, "attention.py")):
+        sys.exit("set REF_DIR to the reference checkout (the directory holding attention.py)")
     ref = load_reference_attention()
     g = torch.Generator().manual_seed(20261201)
     cases = {}
