@@ -1,9 +1,9 @@
 // Single-token decode kernels: fp32 Hadamard rotation, int8 GEMV, split-KV fp32 decode attention.
 //
 // Semantics follow int8_gemv.hip:
-//   rotate      : radix-4 regular-Hadamard stages, stride x4, y[i] = sum - 2 x[3-i], then * rsqrt(group) (:108-129)
-//   gemv_i8     : out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32                         (:131-162)
-//   attn_decode : q * scale, online softmax with expf over a split of ceil(len/32) positions, merge (:198-271)
+//   rotate      : radix-4 regular-Hadamard stages, stride x4, y[i] = sum - 2 x[3-i], then * rsqrt(group) (:32-52)
+//   gemv_i8     : out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32                         (:55-85)
+//   attn_decode : q * scale, online softmax with expf over a split of ceil(len/32) positions, merge (:124-195)
 //
 // The GEMV streams the int8 weight once from HBM with 16-byte non-allocating loads, several rows and
 // several steps in flight per warp. int8 -> fp32 goes through a byte permute into the mantissa of
@@ -452,6 +452,32 @@ extern "C" int b2_decode_qk_rope(const float* qkv, const float* q_norm, const fl
     return check_launch("decode_qk_rope_kernel");
 }
 
+namespace b2 {
+namespace {
+
+bool attn_decode_group_supported(int group) { return group == 1 || group == 2 || group == 4 || group == 8; }
+
+// The split pass and the merge of one decode-attention call, with the partials and statistics at the given device
+// addresses (the caller's scratch, or the library's fixed array). `group` = heads / kv_heads must be supported.
+int launch_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out,
+                       float* partial, float* stats, int batch, int heads, int kv_heads, int capacity, float scale,
+                       cudaStream_t s) {
+    const dim3 grid(DEC_SPLITS, batch * kv_heads);
+    switch (heads / kv_heads) {
+        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        case 8: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
+        default: return fail(B2_ERR_UNSUPPORTED, "attn_decode: %d query heads per KV head", heads / kv_heads);
+    }
+    if (int rc = check_launch("attn_decode_kernel")) return rc;
+    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
+    return check_launch("attn_merge_kernel");
+}
+
+}  // namespace
+}  // namespace b2
+
 extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t* lengths, float* out,
                               float* partial, float* stats, int batch, int heads, int kv_heads, int capacity, float scale,
                               void* stream) {
@@ -459,19 +485,11 @@ extern "C" int b2_attn_decode(const float* q, const float* k, const float* v, co
     if (batch < 0 || heads <= 0 || kv_heads <= 0 || capacity <= 0 || heads % kv_heads)
         return fail(B2_ERR_INVALID, "attn_decode: bad shape");
     const int group = heads / kv_heads;
+    if (!attn_decode_group_supported(group))
+        return fail(B2_ERR_UNSUPPORTED, "attn_decode: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
     if (batch == 0) return B2_OK;
-    dim3 grid(DEC_SPLITS, batch * kv_heads);
-    cudaStream_t s = (cudaStream_t)stream;
-    switch (group) {
-        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 8: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        default: return fail(B2_ERR_UNSUPPORTED, "attn_decode: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
-    }
-    if (int rc = check_launch("attn_decode_kernel")) return rc;
-    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
-    return check_launch("attn_merge_kernel");
+    return launch_attn_decode(q, k, v, lengths, out, partial, stats, batch, heads, kv_heads, capacity, scale,
+                              (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------- decode attention without allocation
@@ -523,24 +541,13 @@ extern "C" int b2_attn_decode_noalloc(const float* q, const float* k, const floa
         return fail(B2_ERR_UNSUPPORTED, "attn_decode_noalloc: batch x heads = %lld exceeds its fixed scratch of %d rows",
                     (long long)batch * heads, NOALLOC_MAX_ROWS);
     const int group = heads / kv_heads;
-    if (group != 1 && group != 2 && group != 4 && group != 8)
+    if (!attn_decode_group_supported(group))
         return fail(B2_ERR_UNSUPPORTED, "attn_decode_noalloc: %d query heads per KV head (supported: 1, 2, 4, 8)", group);
     if (batch == 0) return B2_OK;
     float* scratch = nullptr;
     if (int rc = scratch_for_current_device(&scratch)) return rc;
     // Every (row, split) slot that attn_merge reads is written by attn_decode first, so the array's previous
     // contents never leak into a result and nothing needs clearing.
-    float* partial = scratch;
-    float* stats = scratch + NOALLOC_PARTIAL;
-    dim3 grid(DEC_SPLITS, batch * kv_heads);
-    cudaStream_t s = (cudaStream_t)stream;
-    switch (group) {
-        case 1: attn_decode_kernel<1><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 2: attn_decode_kernel<2><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        case 4: attn_decode_kernel<4><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-        default: attn_decode_kernel<8><<<grid, DEC_WARPS * 32, 0, s>>>(q, k, v, lengths, partial, stats, capacity, kv_heads, scale); break;
-    }
-    if (int rc = check_launch("attn_decode_kernel(noalloc)")) return rc;
-    attn_merge_kernel<<<batch * heads, HEAD, 0, s>>>(partial, stats, out);
-    return check_launch("attn_merge_kernel(noalloc)");
+    return launch_attn_decode(q, k, v, lengths, out, scratch, scratch + NOALLOC_PARTIAL, batch, heads, kv_heads,
+                              capacity, scale, (cudaStream_t)stream);
 }

@@ -164,13 +164,13 @@ int b2_rms_norm_rope(const uint16_t* x, const float* w, uint16_t* y, int rows, i
  * Single-token decode (int8_gemv.hip, launched from int8_gemv.py).
  * ------------------------------------------------------------------------------------------------ */
 /* fp32 regular-Hadamard rotation of each `group` values (power of 4), times rsqrt(group)
- * (int8_gemv.hip:108-129 rotate; int8_gemv.py:42-45). n % group == 0. */
+ * (int8_gemv.hip:32-52 rotate; int8_gemv.py:42-45). n % group == 0. */
 int b2_rotate(const float* x, float* out, int64_t n, int group, void* stream);
-/* out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32 (int8_gemv.hip:131-162 gemv_i8;
+/* out[n] = scale[n] * sum_k w[n,k] x[k] (+ bias[n]), fp32 (int8_gemv.hip:55-85 gemv_i8;
  * int8_gemv.py:62-63). K % 16 == 0. */
 int b2_gemv_i8(const float* x, const int8_t* w, const float* scale, const float* bias, float* out, int N, int K,
                void* stream);
-/* out[n] = sum_k w[n,k] x[k] in fp32 for a bf16 table w [N, K] (int8_gemv.hip:87-119 gemv_bf16; the logits of
+/* out[n] = sum_k w[n,k] x[k] in fp32 for a bf16 table w [N, K] (int8_gemv.hip:88-119 gemv_bf16; the logits of
  * int8_gemv.py:87-98). K % 8 == 0 (the reference: K % 256, N % 16); x and w 16-byte aligned. */
 int b2_gemv_bf16(const float* x, const uint16_t* w, float* out, int N, int K, void* stream);
 /* Decode-step glue of the configuration-5 driver (no counterpart entry points in the reference, whose decode step
@@ -187,7 +187,7 @@ int b2_rms_norm_f32(const float* x, const float* w, float* y, int D, float eps, 
 int b2_decode_qk_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* inv_freq,
                       const int64_t* pos, float* q_out, float* k_cache, float* v_cache, int heads, int kv_heads,
                       float eps, void* stream);
-/* fp32 split-KV decode attention + merge (int8_gemv.hip:198-271 attn_decode/attn_merge;
+/* fp32 split-KV decode attention + merge (int8_gemv.hip:124-180 attn_decode, :183-195 attn_merge;
  * int8_gemv.py:101-114). q [B,1,H,128], k/v [B,capacity,Hkv,128], lengths int32 [B] read on the
  * device (graph-replayable), out [B,1,H,128]. partial: fp32 [B*H, 32, 128], stats: fp32 [B*H, 32, 2]
  * scratch from the caller. */
@@ -198,8 +198,10 @@ int b2_attn_decode(const float* q, const float* k, const float* v, const int32_t
  * memory: hosts whose device memory belongs to another allocator and FFI callers that hold only their own inputs
  * and outputs. The split partials live in a fixed device array inside this library, 2.1 MB on every GPU that loads
  * it, for at most batch x heads = 128 query rows; larger calls return B2_ERR_UNSUPPORTED. The first call on a
- * device looks up that array's address, so make it before any stream capture. All calls share the array: calls that
- * overlap on the GPU (other streams, other threads) race on it. Nothing in it needs to start at zero. */
+ * device looks up that array's address, so make it before any stream capture; the address is then kept for the
+ * life of the process, so a device reset (cudaDeviceReset, a re-created primary context) is not supported after it.
+ * All calls share the array: calls that overlap on the GPU (other streams, other threads) race on it. Nothing in it
+ * needs to start at zero. */
 int b2_attn_decode_noalloc(const float* q, const float* k, const float* v, const int32_t* lengths, float* out, int batch,
                            int heads, int kv_heads, int capacity, float scale, void* stream);
 

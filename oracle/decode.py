@@ -5,7 +5,7 @@ F32 = np.float32
 
 
 def rotate(x, group):
-    """int8_gemv.hip:108-129: radix-4 regular-Hadamard stages with stride 1, 4, 16, ... (the lowest base-4 digit
+    """int8_gemv.hip:32-52: radix-4 regular-Hadamard stages with stride 1, 4, 16, ... (the lowest base-4 digit
     first), y[i] = s - 2 x[3 - i] with s = ((a+b)+c)+d in fp32, then times rsqrt(group) (a power of two)."""
     x = np.asarray(x, F32)
     n = x.size
@@ -23,7 +23,7 @@ def rotate(x, group):
 
 
 def gemv_i8(x, w, scale, bias=None):
-    """out[n] = scale[n] * sum_k w[n, k] x[k] (+ bias[n]) (int8_gemv.hip:131-162), accumulated in float64 here;
+    """out[n] = scale[n] * sum_k w[n, k] x[k] (+ bias[n]) (int8_gemv.hip:55-85), accumulated in float64 here;
     the reference's own fallback is F.linear(x, w.to(fp32) * scale, bias) (int8_gemv.py:58-59)."""
     acc = np.asarray(w, np.float64) @ np.asarray(x, np.float64).reshape(-1)
     y = acc * np.asarray(scale, np.float64)
@@ -38,7 +38,7 @@ def bf16_to_f32(bits):
 
 
 def gemv_bf16(x, w_bits):
-    """out[n] = sum_k w[n, k] x[k] for a bf16 table (int8_gemv.hip:87-119 gemv_bf16, the logits of
+    """out[n] = sum_k w[n, k] x[k] for a bf16 table (int8_gemv.hip:88-119 gemv_bf16, the logits of
     int8_gemv.py:87-98), the table given as uint16 bit patterns, accumulated in float64 here."""
     w = bf16_to_f32(w_bits).astype(np.float64)
     return (w @ np.asarray(x, np.float64).reshape(-1)).astype(F32)
@@ -56,7 +56,7 @@ def linear_fallback(x, w, scale, bias=None):
 
 
 def attn_decode(q, k, v, lengths, scale):
-    """float64 softmax decode attention, the value int8_gemv.hip:198-271 (split-32 online softmax + merge)
+    """float64 softmax decode attention, the value int8_gemv.hip:124-195 (split-32 online softmax + merge)
     approximates in fp32. q [B,1,H,128], k/v [B,cap,Hkv,128], lengths [B]."""
     q = np.asarray(q, np.float64)
     k = np.asarray(k, np.float64)
