@@ -18,27 +18,65 @@ constexpr int DEC_SPLITS = 32;
 constexpr int HEAD = 128;
 
 // ---------------------------------------------------------------- rotate
+// One regular 4-point Hadamard step on (a, b, c, d): s = ((a + b) + c) + d, then (s - 2d, s - 2c, s - 2b, s - 2a).
+__device__ __forceinline__ void h4_step(float& a, float& b, float& c, float& d) {
+    const float s = __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
+    const float a0 = a, b0 = b;
+    a = __fsub_rn(s, __fmul_rn(2.f, d));
+    b = __fsub_rn(s, __fmul_rn(2.f, c));
+    c = __fsub_rn(s, __fmul_rn(2.f, b0));
+    d = __fsub_rn(s, __fmul_rn(2.f, a0));
+}
+
+// One CTA per group of `group` = 4^k values. The k base-4 digit stages (stride 1, 4, 16, ...) run two at a time in
+// registers: a thread takes a 16-value tile (digits 2p and 2p+1 free, the others fixed), applies the stride-4^(2p)
+// step to its four rows and then the stride-4^(2p+1) step to its four columns, which is the stage order of the
+// reference, value for value. The first pass reads the input directly and the last one writes the output (times
+// 1 / sqrt(group), an exact power of two); shared memory holds the group only between passes, so groups of at most
+// 16 values never touch it.
 __global__ void __launch_bounds__(256) rotate_kernel(const float* __restrict__ x, float* __restrict__ out, int group) {
-    extern __shared__ float s[];
+    extern __shared__ float stage_buf[];
     const float* in = x + (int64_t)blockIdx.x * group;
-    for (int i = threadIdx.x; i < group; i += 256) s[i] = in[i];
-    __syncthreads();
-    for (int stride = 1; stride < group; stride *= 4) {
-        for (int q = threadIdx.x; q < group / 4; q += 256) {
-            const int i = (q / stride) * stride * 4 + q % stride;
-            const float a = s[i], b = s[i + stride], c = s[i + 2 * stride], d = s[i + 3 * stride];
-            const float sum = __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
-            s[i] = __fsub_rn(sum, __fmul_rn(2.f, d));
-            s[i + stride] = __fsub_rn(sum, __fmul_rn(2.f, c));
-            s[i + 2 * stride] = __fsub_rn(sum, __fmul_rn(2.f, b));
-            s[i + 3 * stride] = __fsub_rn(sum, __fmul_rn(2.f, a));
-        }
-        __syncthreads();
-    }
-    // group is a power of 4, so the normalisation is an exact power of two.
-    const float norm = __fdiv_rn(1.f, sqrtf((float)group));
     float* o = out + (int64_t)blockIdx.x * group;
-    for (int i = threadIdx.x; i < group; i += 256) o[i] = __fmul_rn(s[i], norm);
+    const int stages = __ffs(group) / 2;  // group = 4^stages
+    const float norm = __fdiv_rn(1.f, sqrtf((float)group));
+    for (int p = 0; 2 * p < stages; ++p) {
+        const int st = 1 << (4 * p);
+        const bool first = p == 0, last = 2 * p + 2 >= stages;
+        const float* src = first ? in : stage_buf;
+        if (2 * p + 1 < stages) {
+            for (int q = threadIdx.x; q < group / 16; q += blockDim.x) {
+                const int base = (q / st) * 16 * st + q % st;
+                float v[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = src[base + (e & 3) * st + (e >> 2) * 4 * st];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) h4_step(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+#pragma unroll
+                for (int a = 0; a < 4; ++a) h4_step(v[a], v[a + 4], v[a + 8], v[a + 12]);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int i = base + (e & 3) * st + (e >> 2) * 4 * st;
+                    if (last) o[i] = __fmul_rn(v[e], norm);
+                    else stage_buf[i] = v[e];
+                }
+            }
+        } else {
+            for (int q = threadIdx.x; q < group / 4; q += blockDim.x) {
+                const int base = (q / st) * 4 * st + q % st;
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[e] = src[base + e * st];
+                h4_step(v[0], v[1], v[2], v[3]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (last) o[base + e * st] = __fmul_rn(v[e], norm);
+                    else stage_buf[base + e * st] = v[e];
+                }
+            }
+        }
+        if (!last) __syncthreads();
+    }
 }
 
 // ---------------------------------------------------------------- gemv_i8
@@ -377,7 +415,7 @@ extern "C" int b2_rotate(const float* x, float* out, int64_t n, int group, void*
         return fail(B2_ERR_UNSUPPORTED, "rotate: group %d must be a power of 4 in [4, 16384]", group);
     if (n % group) return fail(B2_ERR_UNSUPPORTED, "rotate: %lld values is not a multiple of group %d", (long long)n, group);
     if (n == 0) return B2_OK;
-    const int smem = group * 4;
+    const int smem = group > 16 ? group * 4 : 0;  // groups of at most 16 values stay in registers
     if (smem > 48 * 1024)
         if (int rc = set_smem(rotate_kernel, smem)) return rc;
     rotate_kernel<<<(unsigned)(n / group), 256, smem, (cudaStream_t)stream>>>(x, out, group);

@@ -136,6 +136,9 @@ class DiTStack:
     def __init__(self, cfg, plan, device, seed=0, all_gather=None, timer=None):
         self.cfg, self.plan, self.device = cfg, plan, device
         self.timer = timer or (lambda kind, work=0: contextlib.nullcontext())
+        # probe(stage, *tensors), when set, sees each stage's outputs before the next stage overwrites the buffers
+        # they live in (parity tests read sampled rows from them); it adds no launches when unset.
+        self.probe = None
         self.blocks = [DiTBlock(cfg, plan, device, seed * 1000 + i) for i in range(cfg.blocks)]
         self.all_gather = all_gather
         b = plan.batch_hi - plan.batch_lo
@@ -163,12 +166,18 @@ class DiTStack:
         q8 = self.q8[:M * D].view(M, D)
         with t("prepass"):
             ops.mod_quant_pack_a(x.view(M, D), blk.norm1, self.ones, self.zeros, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
+        if self.probe:
+            self.probe("norm1", x.view(M, D), q8, self.sa)
         with t("gemm", 2 * M * D * self.qkv.shape[1]):
             ops.gemm(q8, self.sa, blk.w_qkv, blk.s_qkv, out=self.qkv)
+        if self.probe:
+            self.probe("qkv", self.qkv)
         qkv = self.qkv.view(b, T, 3, hl, cfg.head_dim)
         q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
         with t("attention", 4 * b * hl * T * T * cfg.head_dim):
             ops.attention(q, k, v, self.att.transpose(1, 2), cfg.head_dim ** -0.5)
+        if self.probe:
+            self.probe("attention", self.att)
         return self.att
 
     def mlp_part(self, blk, x, att, gathered=False):
@@ -185,17 +194,29 @@ class DiTStack:
             else:
                 w = att.shape[-1]
                 ops.quant_pack_a_segments(att, D, cfg.rot_group, w, M * w, M, w, out=(q8, self.sa))
+        if self.probe:
+            self.probe("out_prepass", q8, self.sa)
         with t("gemm", 2 * M * D * D):
             ops.gemm(q8, self.sa, blk.w_o, blk.s_o, residual=x2, gate=self.ones, L=T, out=self.xa)
+        if self.probe:
+            self.probe("out_proj", self.xa)
         with t("prepass"):
             ops.mod_quant_pack_a(self.xa, blk.norm2, self.ones, self.zeros, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
+        if self.probe:
+            self.probe("norm2", q8, self.sa)
         with t("gemm", 2 * M * D * 2 * F):
             ops.gemm_swiglu(q8, self.sa, blk.w_gu, blk.s_gu, out=self.act)
+        if self.probe:
+            self.probe("gate_up", self.act)
         q8f = self.q8[:M * F].view(M, F)
         with t("prepass"):
             ops.quant_pack_a(self.act, cfg.rot_group, out=(q8f, self.sa))
+        if self.probe:
+            self.probe("down_prepass", q8f, self.sa)
         with t("gemm", 2 * M * F * D):
             ops.gemm(q8f, self.sa, blk.w_down, blk.s_down, residual=self.xa, gate=self.ones, L=T, out=x2)
+        if self.probe:
+            self.probe("down", x2)
         return x
 
     def block(self, blk, x):
