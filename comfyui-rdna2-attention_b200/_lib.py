@@ -32,6 +32,7 @@ SIGNATURES = {
     "b2_gemm_i32": (I, [P, P, P, I, I, I, P]),
     "b2_gemm_swiglu": (I, [P, P, P, P, P, I, I, I, P]),
     "b2_gemm_w4a8": (I, [P, P, P, P, P, P, I, I, I, P]),
+    "b2_gemm_w4a8_wide": (I, [P, P, P, P, P, P, I, I, I, P]),
     "b2_quant_pack_a_i4": (I, [P, I64, P, P, I, I, I, P]),
     "b2_unpack_int4": (I, [P, P, I, I, P]),
     "b2_gemm_w4a4": (I, [P, P, P, P, P, P, I, I, I, P, P]),

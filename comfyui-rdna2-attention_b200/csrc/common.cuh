@@ -253,6 +253,15 @@ __device__ __forceinline__ void tmem_ld16_wait(uint32_t taddr, uint32_t (&r)[16]
         : "r"(taddr)
         : "memory");
 }
+// 8 consecutive 32-bit columns of the warp's 32 lanes, loaded and waited for in one asm statement.
+__device__ __forceinline__ void tmem_ld8_wait(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+}
 // 32 consecutive columns of the warp's 32 lanes all set to `v` (one source register).
 __device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
     asm volatile(
@@ -336,6 +345,11 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Arrival with release semantics at cluster scope: this thread's earlier shared-memory writes (made visible to the
+// tensor core by fence.proxy.async) happen before whatever the waiter on the barrier does next.
+__device__ __forceinline__ void mbar_arrive_remote_release(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx_remote(uint32_t cluster_addr, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
                  "r"(bytes)
@@ -375,6 +389,13 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
+
+// Per-warpgroup register budgets (all four warps of a warpgroup execute the same one). The sum over the CTA's
+// warpgroups must stay within the registers the CTA was launched with, or an increase never completes.
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
 // ---------------------------------------------------------------- packed fp32 pairs (sm_100 f32x2)
 // Each lane of an f32x2 operation rounds exactly like the scalar fp32 operation.

@@ -247,12 +247,16 @@ def _packed_int4(w_packed, K, name):
         _fail(f"{name}: the packed weight has {w_packed.shape[1] * 2} values per row, the activations {K}")
 
 
-def gemm_w4a8(a_q, a_scale, w_packed, gscale, bias=None, out=None):
+def gemm_w4a8(a_q, a_scale, w_packed, gscale, bias=None, out=None, w_wide=None):
     """fp16 [M, N] = sum over groups of int32 (a_q . w^T)_g * gscale[g, n], times a_scale[m] (+ bias).
-    w_packed uint8 [N, K/2] (low nibble = even k); gscale fp32 [K/128, N] (see w4a8_scales)."""
+    w_packed uint8 [N, K/2] (low nibble = even k); gscale fp32 [K/128, N] (see w4a8_scales). ``w_wide``, the same
+    weight widened to int8 [N, K] (unpack_int4), selects the kernel that reads it instead; the result is the same
+    bit for bit."""
     M, K = _int8_rows(a_q, "gemm_w4a8")
     _packed_int4(w_packed, K, "gemm_w4a8")
     N = w_packed.shape[0]
+    if w_wide is not None and (w_wide.dtype != torch.int8 or tuple(w_wide.shape) != (N, K) or not w_wide.is_contiguous()):
+        _fail(f"gemm_w4a8: the widened weight must be contiguous int8 [{N}, {K}]")
     _vec(a_scale, M, torch.float32, "gemm_w4a8 activation scale")
     if gscale.dtype != torch.float32 or tuple(gscale.shape) != (K // 128, N) or not gscale.is_contiguous():
         _fail("gemm_w4a8 scales must be contiguous fp32 [K/128, N]")
@@ -260,9 +264,13 @@ def gemm_w4a8(a_q, a_scale, w_packed, gscale, bias=None, out=None):
     _exact(out, (M, N), torch.float16, "gemm_w4a8 output")
     if out is None:
         out = torch.empty((M, N), dtype=torch.float16, device=a_q.device)
-    require_cuda(a_q, a_scale, w_packed, gscale, bias, out)
-    call("b2_gemm_w4a8", ptr(a_q), ptr(w_packed), ptr(a_scale), ptr(gscale), ptr(bias), ptr(out), I(M), I(N), I(K),
-         stream())
+    require_cuda(a_q, a_scale, w_packed, gscale, bias, out, w_wide)
+    if w_wide is not None:
+        call("b2_gemm_w4a8_wide", ptr(a_q), ptr(w_wide), ptr(a_scale), ptr(gscale), ptr(bias), ptr(out), I(M), I(N),
+             I(K), stream())
+    else:
+        call("b2_gemm_w4a8", ptr(a_q), ptr(w_packed), ptr(a_scale), ptr(gscale), ptr(bias), ptr(out), I(M), I(N),
+             I(K), stream())
     return out
 
 

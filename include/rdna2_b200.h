@@ -132,6 +132,11 @@ int b2_gemm_w4a4(const int8_t* A, const uint8_t* Wp, const float* as, const floa
  * ------------------------------------------------------------------------------------------------ */
 int b2_gemm_w4a8(const int8_t* A, const uint8_t* Wp, const float* as, const float* gscale, const uint16_t* bias,
                  uint16_t* C, int M, int N, int K, void* stream);
+/* b2_gemm_w4a8 on a weight already widened to int8 W [N, K] (values in [-8, 7]), e.g. by b2_unpack_int4: the
+ * unpacked-weight form that convrot_w4a4_forward's qweight_unpacked argument carries (int8_gemm.py:91). Same
+ * arithmetic and result bit for bit; the tile no longer waits on on-chip widening. */
+int b2_gemm_w4a8_wide(const int8_t* A, const int8_t* W, const float* as, const float* gscale, const uint16_t* bias,
+                      uint16_t* C, int M, int N, int K, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Fused attention, head dim 128, no mask. Replaces hip_attention.hip pack_kv + attn (:32,:280) and

@@ -212,10 +212,18 @@ def test_prefill_routes_while_generating(pkg, calls):
 
 
 def test_w4a8_forward_dispatch(pkg, calls):
-    """int8_gemm.w4a8_forward: block-128 rotation + int8 pre-pass, then the group-128 W4A8 GEMM."""
+    """int8_gemm.w4a8_forward: block-128 rotation + int8 pre-pass, then the group-128 W4A8 GEMM on the widened weight
+    (widened per call, or the caller's qweight_unpacked as is)."""
     f = pkg.int8_gemm.w4a8_forward
     x = torch.randn((2, 7, 512)).half()
     out = f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones((64, 4)).half(), None, 128, torch.float16)
-    assert out.shape == (2, 7, 64) and calls == ["b2_quant_pack_a", "b2_gemm_w4a8"]
+    assert out.shape == (2, 7, 64) and calls == ["b2_unpack_int4", "b2_quant_pack_a", "b2_gemm_w4a8_wide"]
+    calls.clear()
+    out = f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones((64, 4)).half(), None, 128, torch.float16,
+            qweight_unpacked=torch.zeros((64, 512), dtype=torch.int8))
+    assert out.shape == (2, 7, 64) and calls == ["b2_quant_pack_a", "b2_gemm_w4a8_wide"]
+    with pytest.raises(NotImplementedError, match="qweight_unpacked"):
+        f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones((64, 4)).half(), None, 128, torch.float16,
+          qweight_unpacked=torch.zeros((64, 256), dtype=torch.int8))
     with pytest.raises(NotImplementedError, match="scales of shape"):
         f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones(64).half(), None, 128, torch.float16)

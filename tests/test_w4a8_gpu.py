@@ -1,6 +1,7 @@
 """W4A8 (group-128) GEMM parity on the GPU against the specification oracle (oracle.gemm.w4a8_grouped): int32 per
-group, F = fma(acc_g, s_g, F) in fp32, y = F * sa (+ bias) -> fp16. Compared bit for bit; the configuration-3 linear
-(M=2809, K=3072, N=8192, block-128 rotated int8 activations) end to end."""
+group, F = fma(acc_g, s_g, F) in fp32, y = F * sa (+ bias) -> fp16. Compared bit for bit, for both kernels: the one
+that widens the packed weight in shared memory and the one that reads a widened int8 copy; the configuration-3
+linear (M=2809, K=3072, N=8192, block-128 rotated int8 activations) end to end."""
 import numpy as np
 import pytest
 import torch
@@ -29,14 +30,19 @@ def case(M, N, K, seed):
     return a, sa, packed, s16, bias
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 8, 128), (100, 136, 256), (257, 512, 1024), (128, 128, 3072), (1000, 264, 640)])
-def test_w4a8_matches_spec(pkg, dev, M, N, K):
+@pytest.mark.parametrize("wide", [False, True])
+@pytest.mark.parametrize("M,N,K", [(1, 8, 128), (100, 136, 256), (257, 512, 1024), (128, 128, 3072), (1000, 264, 640),
+                                   (300, 520, 384)])
+def test_w4a8_matches_spec(pkg, dev, M, N, K, wide):
     a, sa, packed, s16, bias = case(M, N, K, M + N + K)
     gs = pkg.ops.w4a8_scales(dev_(s16, dev))
+    wp = dev_(packed, dev)
+    ww = pkg.ops.unpack_int4(wp) if wide else None
     for b in (None, bias):
-        got = pkg.ops.gemm_w4a8(dev_(a, dev), dev_(sa, dev), dev_(packed, dev), gs, None if b is None else dev_(b, dev))
+        got = pkg.ops.gemm_w4a8(dev_(a, dev), dev_(sa, dev), wp, gs, None if b is None else dev_(b, dev), w_wide=ww)
         ref = ogemm.w4a8_grouped(a, sa, packed, s16, bias=b)
         assert np.array_equal(got.cpu().numpy(), ref)
+    assert pkg._lib.device_status() == 0
 
 
 def test_w4a8_extreme_nibbles(pkg, dev):
@@ -46,9 +52,11 @@ def test_w4a8_extreme_nibbles(pkg, dev):
     packed[1] = 0x77                                  # every weight 7
     s16 = np.ones((N, K // 128), F16)
     sa = np.ones(M, F32)
-    got = pkg.ops.gemm_w4a8(dev_(a, dev), dev_(sa, dev), dev_(packed, dev), pkg.ops.w4a8_scales(dev_(s16, dev)))
+    wp, gs = dev_(packed, dev), pkg.ops.w4a8_scales(dev_(s16, dev))
     ref = ogemm.w4a8_grouped(a, sa, packed, s16)
-    assert np.array_equal(got.cpu().numpy(), ref)
+    for ww in (None, pkg.ops.unpack_int4(wp)):
+        got = pkg.ops.gemm_w4a8(dev_(a, dev), dev_(sa, dev), wp, gs, w_wide=ww)
+        assert np.array_equal(got.cpu().numpy(), ref)
 
 
 def test_config3_linear(pkg, dev):
@@ -60,11 +68,14 @@ def test_config3_linear(pkg, dev):
     w = (g.standard_normal((N, K)) * 0.02).astype(F32)
     packed, s16 = ow.quantize_int4_groups(ow.sylvester_rotate(w))
     q, s = pkg.ops.quant_pack_a(dev_(x, dev), 128)
-    got = pkg.ops.gemm_w4a8(q, s, dev_(packed, dev), pkg.ops.w4a8_scales(dev_(s16, dev))).cpu().numpy()
+    wp, gs = dev_(packed, dev), pkg.ops.w4a8_scales(dev_(s16, dev))
+    got = pkg.ops.gemm_w4a8(q, s, wp, gs).cpu().numpy()
+    got_wide = pkg.ops.gemm_w4a8(q, s, wp, gs, w_wide=pkg.ops.unpack_int4(wp)).cpu().numpy()
     q_ref, s_ref, _ = oq.prepass(x, 128)
     assert np.array_equal(q.cpu().numpy(), q_ref)
     ref = ogemm.w4a8_grouped(q_ref, s_ref, packed, s16)
     assert np.array_equal(got, ref)
+    assert np.array_equal(got_wide, ref)
     exact = x.astype(np.float64) @ w.T.astype(np.float64)
     assert np.linalg.norm(got - exact) / np.linalg.norm(exact) < 0.15  # int4 weight error, for scale
 
