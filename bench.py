@@ -279,13 +279,14 @@ class GemmC1:
         x = g.standard_normal((M, K)).astype(np.float16)
         wq, ws = ow.quantize_per_channel(ow.sylvester_rotate((g.standard_normal((N, K)) * 0.02).astype(np.float32)))
         bias = (g.standard_normal(N) * 0.01).astype(np.float16)
-        reps, t0 = 0, time.perf_counter()
-        while reps < 3 or time.perf_counter() - t0 < 10:
+
+        def run():
+            t0 = time.perf_counter()
             q, s, _ = oq.prepass(x, 128)
             ogemm.epilogue(ogemm.int_mm(q, wq), s, ws, bias)
-            reps += 1
-        dt = (time.perf_counter() - t0) / reps
-        return 2.0 * M * N * K / dt / 1e12, f"{reps} full C1 linears (oracle pre-pass + torch._int_mm + epilogue)"
+            dt = time.perf_counter() - t0
+            return 2.0 * M * N * K / dt / 1e12, dt
+        return run, "one full C1 linear per sample (oracle pre-pass + torch._int_mm + epilogue), scale 1"
 
 
 class AttnC2:
@@ -355,13 +356,14 @@ class AttnC2:
         B, H, S = AttnC2.B, AttnC2.H, AttnC2.S
         gen = torch.Generator().manual_seed(2)
         q, k, v = (torch.randn((1, 1, S, 128), generator=gen).half() for _ in range(3))
-        reps, t0 = 0, time.perf_counter()
-        while reps < 3 or time.perf_counter() - t0 < 10:
+
+        def run():
+            t0 = time.perf_counter()
             oatt.attention_bmm(q, k, v)
-            reps += 1
-        dt = (time.perf_counter() - t0) / reps
-        flops = 4.0 * S * S * 128
-        return flops / dt / 1e12, f"{reps} single (batch, head) slices of C2 through the reference's attention_bmm (fp16 CPU), scaled per slice"
+            dt = time.perf_counter() - t0
+            return 4.0 * S * S * 128 / dt / 1e12, dt
+        return run, (f"one (batch, head) slice of C2 per sample through the reference's attention_bmm (fp16 CPU); "
+                     f"TFLOPS per slice = TFLOPS of the {B * H}-slice call")
 
 
 class W4A8C3:
@@ -442,11 +444,14 @@ class W4A8C3:
         M, K, N = 512, W4A8C3.K, W4A8C3.N
         x = g.standard_normal((M, K)).astype(np.float16)
         packed, s16 = ow.quantize_int4_groups((g.standard_normal((N, K)) * 0.02).astype(np.float32))
-        t0 = time.perf_counter()
-        q, s, _ = oq.prepass(x, 128)
-        ogemm.w4a8_grouped(q, s, packed, s16)
-        dt = time.perf_counter() - t0
-        return 2.0 * M * N * K / dt / 1e12, "512 of the 2809 rows through the oracle pre-pass + per-group torch._int_mm + fp32 combine"
+
+        def run():
+            t0 = time.perf_counter()
+            q, s, _ = oq.prepass(x, 128)
+            ogemm.w4a8_grouped(q, s, packed, s16)
+            dt = time.perf_counter() - t0
+            return 2.0 * M * N * K / dt / 1e12, dt
+        return run, "512 of the 2809 rows per sample (oracle pre-pass + per-group torch._int_mm + fp32 combine); TOPS of the sample"
 
 
 class W4A4C3(W4A8C3):
@@ -513,11 +518,14 @@ class W4A4C3(W4A8C3):
         x = g.standard_normal((M, K)).astype(np.float16)
         packed = g.integers(0, 256, (N, K // 2), dtype=np.uint8)
         ws = np.full(N, 1e-3, np.float32)
-        t0 = time.perf_counter()
-        q, s = oq.quant_rows_i4(oq.rotate_rows(x, 256))
-        ogemm.epilogue(ogemm.int_mm(q, ogemm.unpack_int4(packed)), s, ws)
-        dt = time.perf_counter() - t0
-        return 2.0 * M * N * K / dt / 1e12, "512 of the 2809 rows through the oracle ConvRot + int4 quant + torch._int_mm + epilogue"
+
+        def run():
+            t0 = time.perf_counter()
+            q, s = oq.quant_rows_i4(oq.rotate_rows(x, 256))
+            ogemm.epilogue(ogemm.int_mm(q, ogemm.unpack_int4(packed)), s, ws)
+            dt = time.perf_counter() - t0
+            return 2.0 * M * N * K / dt / 1e12, dt
+        return run, "512 of the 2809 rows per sample (oracle ConvRot + int4 quant + torch._int_mm + epilogue); TOPS of the sample"
 
 
 class GemmQKV(GemmC1):
@@ -528,9 +536,7 @@ class GemmQKV(GemmC1):
     config = {"workload": "C4 QKV projection", "M": 6642, "K": 3072, "N": 9216, "rotation": "block-128 Sylvester",
               "l2": "rotating input/weight sets > 2x L2"}
 
-    @staticmethod
-    def cpu_baseline(threads):
-        return None, "not measured for this single-kernel case"
+    cpu_baseline = None
 
 
 class PrepassC4:
@@ -595,11 +601,14 @@ class PrepassC4:
         g = np.random.default_rng(6)
         M, K = 512, PrepassC4.K
         x = g.standard_normal((M, K)).astype(np.float16)
-        t0 = time.perf_counter()
-        oq.prepass(x, 128, act="mod", w=np.zeros(K, np.float32), s=np.ones((1, K), np.float16),
-                   t=np.zeros((1, K), np.float16), L=M)
-        dt = time.perf_counter() - t0
-        return (M * K * 3 + M * 4) / dt / 1e9, "512 of 6642 rows through the numpy oracle pre-pass"
+
+        def run():
+            t0 = time.perf_counter()
+            oq.prepass(x, 128, act="mod", w=np.zeros(K, np.float32), s=np.ones((1, K), np.float16),
+                       t=np.zeros((1, K), np.float16), L=M)
+            dt = time.perf_counter() - t0
+            return (M * K * 3 + M * 4) / dt / 1e9, dt
+        return run, "512 of 6642 rows per sample through the numpy oracle pre-pass; GB/s of the sample"
 
 
 class DecodeC5:
@@ -675,16 +684,18 @@ class DecodeC5:
         ws = [(torch.randint(-127, 128, s, generator=g, dtype=torch.int8), torch.rand(s[0], generator=g) * 1e-3) for s in shapes]
         kc = torch.randn((1024, 8, 128), generator=g)
         vc = torch.randn((1024, 8, 128), generator=g)
-        x = torch.randn((1, D), generator=g)
-        t0 = time.perf_counter()
-        for _ in range(4):
-            for w, sc in ws:
-                Fn.linear(torch.randn((1, w.shape[1]), generator=g), w.to(torch.float32) * sc[:, None])
-            q = torch.randn((32, 128), generator=g)
-            s_ = torch.einsum("hd,khd->hk", q, kc.repeat_interleave(4, 1)) * 128 ** -0.5
-            torch.softmax(s_, -1) @ vc.repeat_interleave(4, 1).transpose(0, 1)
-        dt = (time.perf_counter() - t0) / 4 * 36
-        return dt * 1e3, "4 of 36 layers through the reference's F.linear(x, w.float() * scale) fallback + fp32 softmax attention, scaled to 36 layers"
+        def run():
+            t0 = time.perf_counter()
+            for _ in range(4):
+                for w, sc in ws:
+                    Fn.linear(torch.randn((1, w.shape[1]), generator=g), w.to(torch.float32) * sc[:, None])
+                q = torch.randn((32, 128), generator=g)
+                s_ = torch.einsum("hd,khd->hk", q, kc.repeat_interleave(4, 1)) * 128 ** -0.5
+                torch.softmax(s_, -1) @ vc.repeat_interleave(4, 1).transpose(0, 1)
+            dt = time.perf_counter() - t0
+            return dt / 4 * 36 * 1e3, dt
+        return run, ("4 of 36 layers per sample through the reference's F.linear(x, w.float() * scale) fallback + fp32 "
+                     "softmax attention; ms of the sample x 36 / 4")
 
 
 class LogitsC5:
@@ -747,12 +758,13 @@ class LogitsC5:
         rows = 16384
         table = (torch.randn((rows, LogitsC5.K), generator=g) * 0.02).to(torch.bfloat16)
         x = torch.randn((1, LogitsC5.K), generator=g)
-        t0 = time.perf_counter()
-        reps = 3
-        for _ in range(reps):
+
+        def run():
+            t0 = time.perf_counter()
             Fn.linear(x, table.float())
-        dt = (time.perf_counter() - t0) / reps * LogitsC5.N / rows
-        return (LogitsC5.N * LogitsC5.K * 2) / dt / 1e9, "16384 of 151936 rows, F.linear(x, table.float()), scaled"
+            dt = time.perf_counter() - t0
+            return (rows * LogitsC5.K * 2) / dt / 1e9, dt
+        return run, "16384 of 151936 rows per sample, F.linear(x, table.float()); GB/s of the sample"
 
 
 class KindTimer:
@@ -910,38 +922,58 @@ class DiTC4:
 
     @staticmethod
     def cpu_baseline(threads):
-        """One block of the reference's CPU path on a sample (512 of the 6642 rows through the W8A8 linears, 2 of the 48
-        (batch, head) attention slices through attention_bmm), scaled to the 8-block step."""
+        """One block of the reference's CPU path on a sample (1024 of the 6642 rows through the W8A8 linears, 2 of the
+        48 (batch, head) attention slices through attention_bmm), scaled to the 8-block step."""
         from oracle import attention as oatt
         from oracle import gemm as ogemm
         from oracle import quant as oq
 
         torch.set_num_threads(threads)
         g = np.random.default_rng(0)
-        D, F, T, Ms = 3072, 8192, 3321, 512
+        D, F, T, Ms = 3072, 8192, 3321, 1024
         w = {n: g.integers(-127, 128, s, dtype=np.int8) for n, s in
              {"qkv": (3 * D, D), "o": (D, D), "gu": (2 * F, D), "down": (D, F)}.items()}
         ws = {n: np.full(v.shape[0], 1e-3, np.float32) for n, v in w.items()}
         x = g.standard_normal((Ms, D)).astype(np.float16)
         ones, zeros = np.ones((1, D), np.float16), np.zeros((1, D), np.float16)
         nw = np.zeros(D, np.float32)
-        t0 = time.perf_counter()
-        q, s = oq.quant_rows(oq.rotate_rows(oq.modulate(x, nw, ones, zeros, Ms, 1e-6), 128))
-        ogemm.epilogue(ogemm.int_mm(q, w["qkv"]), s, ws["qkv"])
-        q, s = oq.quant_rows(oq.rotate_rows(x, 128))
-        xa = ogemm.epilogue(ogemm.int_mm(q, w["o"]), s, ws["o"], R=x, G=ones, L=Ms)
-        q, s = oq.quant_rows(oq.rotate_rows(oq.modulate(xa, nw, ones, zeros, Ms, 1e-6), 128))
-        gu = ogemm.epilogue(ogemm.int_mm(q, w["gu"]), s, ws["gu"])
-        q, s = oq.quant_rows(oq.rotate_rows(oq.swiglu(gu[:, :F], gu[:, F:]), 128))
-        ogemm.epilogue(ogemm.int_mm(q, w["down"]), s, ws["down"], R=xa, G=ones, L=Ms)
-        t_lin = time.perf_counter() - t0
         gen = torch.Generator().manual_seed(2)
         qa, ka, va = (torch.randn((1, 2, T, 128), generator=gen).half() for _ in range(3))
-        t0 = time.perf_counter()
-        oatt.attention_bmm(qa, ka, va)
-        t_att = time.perf_counter() - t0
-        ms = 8 * (t_lin * (2 * T / Ms) + t_att * (48 / 2)) * 1e3
-        return ms, "one block: 512 of 6642 rows through the 4 W8A8 linears (oracle pre-pass + torch._int_mm + epilogue) and 2 of 48 (batch, head) attention slices (attention_bmm, fp16), scaled to 8 blocks"
+        lin_scale, att_scale = 2 * T / Ms, 24
+
+        def run():
+            t0 = time.perf_counter()
+            q, s = oq.quant_rows(oq.rotate_rows(oq.modulate(x, nw, ones, zeros, Ms, 1e-6), 128))
+            ogemm.epilogue(ogemm.int_mm(q, w["qkv"]), s, ws["qkv"])
+            q, s = oq.quant_rows(oq.rotate_rows(x, 128))
+            xa = ogemm.epilogue(ogemm.int_mm(q, w["o"]), s, ws["o"], R=x, G=ones, L=Ms)
+            q, s = oq.quant_rows(oq.rotate_rows(oq.modulate(xa, nw, ones, zeros, Ms, 1e-6), 128))
+            gu = ogemm.epilogue(ogemm.int_mm(q, w["gu"]), s, ws["gu"])
+            q, s = oq.quant_rows(oq.rotate_rows(oq.swiglu(gu[:, :F], gu[:, F:]), 128))
+            ogemm.epilogue(ogemm.int_mm(q, w["down"]), s, ws["down"], R=xa, G=ones, L=Ms)
+            t_lin = time.perf_counter() - t0
+            t1 = time.perf_counter()
+            oatt.attention_bmm(qa, ka, va)
+            t_att = time.perf_counter() - t1
+            return 8 * (t_lin * lin_scale + t_att * att_scale) * 1e3, t_lin + t_att
+        return run, (f"per sample, one block: 1024 of 6642 rows through the 4 W8A8 linears (oracle pre-pass + "
+                     f"torch._int_mm + epilogue; time x {lin_scale:.2f}) and 2 of 48 (batch, head) attention slices "
+                     f"(the reference's attention_bmm, fp16; time x 24), x 8 blocks")
+
+
+def cpu_measure(baseline, threads, reps, warmup=1):
+    """Times a workload's CPU sample `reps` times after `warmup` untimed runs; the value is the median of the
+    samples' scaled values. Returns (value, description with the measured seconds)."""
+    run, desc = baseline(threads)
+    for _ in range(warmup):
+        run()
+    vals, secs = [], []
+    for _ in range(reps):
+        v, dt = run()
+        vals.append(v)
+        secs.append(dt)
+    return float(np.median(vals)), (f"{desc}. {reps} timed samples after {warmup} untimed: median {float(np.median(secs)):.3f} s "
+                                    f"per sample (min {min(secs):.3f}, max {max(secs):.3f}), median value taken")
 
 
 WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4,
@@ -950,37 +982,42 @@ WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, 
 
 
 def reference_arm(args, world, rank):
+    """The reference's CPU path (restated: the oracle port, kind "port") on the host cores: W untimed and K timed
+    samples of the workload, each scaled to the metric's unit; the value is the median. The reference's own kernels
+    also compile for the host (oracle/_ref), but as an emulation of its GPU threads they are a checker, not the
+    reference's CPU path, and are not timed here."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     name = args.workload
+    meas = lambda baseline: cpu_measure(baseline, threads, max(args.steps, 3), args.warmup)  # noqa: E731
     if name == "gemm":
-        v, sample = GemmC1.cpu_baseline(threads)
+        v, sample = meas(GemmC1.cpu_baseline)
         metric, unit, higher, cfg = GemmC1.metric, GemmC1.unit, True, GemmC1.config
     elif name in ("attn", "attn_i8"):
-        v, sample = AttnC2.cpu_baseline(threads, name == "attn_i8")
+        v, sample = meas(lambda t: AttnC2.cpu_baseline(t, name == "attn_i8"))
         w = AttnC2.__new__(AttnC2)
         metric = f"attention TFLOPS (C2: B2 H24 S4056 d128, {'int8' if name == 'attn_i8' else 'fp16'} QK)"
         unit, higher = "TFLOPS", True
         cfg = {"workload": "C2 fused attention", "B": 2, "H": 24, "S": 4056, "d": 128}
     elif name == "w4a8":
-        v, sample = W4A8C3.cpu_baseline(threads)
+        v, sample = meas(W4A8C3.cpu_baseline)
         metric, unit, higher, cfg = W4A8C3.metric, W4A8C3.unit, True, {"workload": "C3 W4A8 linear", "M": 2809,
                                                                          "K": 3072, "N": 8192, "group": 128}
     elif name == "decode":
-        v, sample = DecodeC5.cpu_baseline(threads)
+        v, sample = meas(DecodeC5.cpu_baseline)
         metric, unit, higher = DecodeC5.metric, DecodeC5.unit, False
         cfg = {"workload": "C5 single-token decode", "layers": 36, "hidden": 2560, "kv_len": 1024}
     elif name == "w4a4":
-        v, sample = W4A4C3.cpu_baseline(threads)
+        v, sample = meas(W4A4C3.cpu_baseline)
         metric, unit, higher = W4A4C3.metric, W4A4C3.unit, True
         cfg = {"workload": "C3 shapes, per-channel W4A4", "M": W4A4C3.M, "K": W4A4C3.K, "N": W4A4C3.N}
     elif name == "logits":
-        v, sample = LogitsC5.cpu_baseline(threads)
+        v, sample = meas(LogitsC5.cpu_baseline)
         metric, unit, higher = LogitsC5.metric, LogitsC5.unit, True
         cfg = {"workload": "C5 logits (tied bf16 embedding table)", "N": LogitsC5.N, "K": LogitsC5.K}
     elif name == "dit":
-        v, sample = DiTC4.cpu_baseline(threads)
+        v, sample = meas(DiTC4.cpu_baseline)
         metric, unit, higher = DiTC4.metric, DiTC4.unit, False
         cfg = {"workload": "C4 DiT block stack", "blocks": 8, "batch": 2, "tokens": 3321, "hidden": 3072, "heads": 24,
                "mlp": 8192}
@@ -1045,8 +1082,8 @@ def main():
                     "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes},
             "roofline": wl.roofline(peaks, kms), "kernel_ms": kms, "clocks": clocks.summary(),
             "gpu_launches": wl.launches_per_step * args.steps}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, sample = type(wl).cpu_baseline(os.cpu_count() or 1) if hasattr(type(wl), "cpu_baseline") else (None, "")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and getattr(type(wl), "cpu_baseline", None):
+        v, sample = cpu_measure(type(wl).cpu_baseline, os.cpu_count() or 1, 3)
         line["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": os.cpu_count(), "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps(line))
