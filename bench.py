@@ -824,9 +824,14 @@ class DiTC4:
                     groups[gr] = dist.new_group(list(gr)) if len(gr) > 1 else None
             pg = groups[plan.group_ranks]
         gather = (lambda out, inp: dist.all_gather_into_tensor(out, inp, group=pg)) if pg is not None else None
-        self.timer = KindTimer()
-        self.stack = dit.DiTStack(cfg, plan, dev, seed=0, all_gather=gather, timer=self.timer)
         b = plan.batch_hi - plan.batch_lo
+        self.fused = None
+        if pg is not None and GATHER == "fused":
+            # The head-group exchange fused into the attention (peer stores + arrival counters in symmetric memory).
+            self.fused = dit.FusedGather.create(pg, plan.group_index, plan.group_size, b, cfg.tokens,
+                                                (plan.head_hi - plan.head_lo) * cfg.head_dim, dev)
+        self.timer = KindTimer()
+        self.stack = dit.DiTStack(cfg, plan, dev, seed=0, all_gather=gather, timer=self.timer, fused_gather=self.fused)
         gen = torch.Generator().manual_seed(4)
         x_all = torch.randn((cfg.batch, cfg.tokens, cfg.hidden), generator=gen).half()
         self.x_host = x_all[plan.batch_lo:plan.batch_hi].contiguous().pin_memory()
@@ -844,7 +849,10 @@ class DiTC4:
                        "e2e": "per step: pinned host input -> device and result -> pinned host on a copy stream, the next "
                               "step's input and the previous step's result overlapping this step's compute",
                        "shard": {"branches": [plan.batch_lo, plan.batch_hi], "heads": [plan.head_lo, plan.head_hi],
-                                 "group": list(plan.group_ranks)}}
+                                 "group": list(plan.group_ranks)},
+                       "head_group_exchange": ("none" if pg is None else
+                                               "fused into the attention (peer stores, symmetric memory)"
+                                               if self.fused is not None else "NCCL all_gather_into_tensor")}
 
     def step(self, i, record=False):
         self.x.copy_(self.x0)
@@ -976,6 +984,8 @@ def cpu_measure(baseline, threads, reps, warmup=1):
                                     f"per sample (min {min(secs):.3f}, max {max(secs):.3f}), median value taken")
 
 
+GATHER = "fused"  # head-group exchange of the sharded DiT stack: "fused" or "nccl" (--gather)
+
 WORKLOADS = {"gemm": GemmC1, "attn": AttnC2, "attn_i8": lambda dev: AttnC2(dev, int8_qk=True), "dit": DiTC4,
              "w4a8": W4A8C3, "gemm_qkv": GemmQKV, "prepass": PrepassC4, "decode": DecodeC5,
              "logits": LogitsC5, "w4a4": W4A4C3}
@@ -1039,7 +1049,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="dit", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
+                    help="head-group exchange of the sharded DiT stack (4 or 8 GPUs)")
     args = ap.parse_args()
+    global GATHER
+    GATHER = args.gather
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
@@ -1085,8 +1099,18 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline and getattr(type(wl), "cpu_baseline", None):
         v, sample = cpu_measure(type(wl).cpu_baseline, os.cpu_count() or 1, 3)
         line["cpu_baseline"] = {"value": v, "unit": wl.unit, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+    fused = getattr(wl, "fused", None)
+    if fused is not None:
+        torch.cuda.synchronize()
+        if fused.failed():
+            raise RuntimeError(f"rank {rank}: a head-group gather wait ran out (a peer stopped delivering)")
     if rank == 0:
         print(json.dumps(line))
+    if fused is not None:
+        wl.stack.fused = wl.fused = None
+        del fused
+        torch.cuda.synchronize()
+        barrier(world)
     if world > 1 and dist.is_initialized():
         dist.destroy_process_group()
 

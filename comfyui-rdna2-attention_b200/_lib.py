@@ -39,6 +39,10 @@ SIGNATURES = {
     "b2_attention_workspace_bytes": (I64, [I, I, I, I, I, I]),
     "b2_attention": (I, [P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
                          I, I, I, I, I, F, I, P, I64, P]),
+    "b2_attention_gather": (I, [P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
+                                I, I, I, I, I, F, I, P, I64, P, P, I, P]),
+    "b2_attention_gather_ctas": (I, [I, I, I]),
+    "b2_wait_count": (I, [P, ctypes.c_ulonglong, P, ctypes.c_longlong, P]),
     "b2_rms_norm": (I, [P, P, P, I, I, I, I, I64, I64, I64, F, P]),
     "b2_rms_norm_rope": (I, [P, P, P, I, I, I, I, I64, I64, I64, F, P, I64, P]),
     "b2_rotate": (I, [P, P, I64, I, P]),

@@ -41,9 +41,16 @@ struct AttCfg {
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
 };
 
+constexpr int MAX_PEERS = 7;
+
 struct AttArgs {
     __half* out;
     int64_t sob, soh, sol;
+    // Head-group gather: the same output tile also goes to these peers' buffers at the same offsets (their memory
+    // mapped into this GPU's address space), and each finished CTA adds 1 to every peer's arrival counter.
+    __half* peer_out[MAX_PEERS];
+    unsigned long long* peer_cnt[MAX_PEERS];
+    int npeer;
     const float* qscale;  // int8: [B*H, Lq]
     int Lq, Lk, H, rep;
     float scale_log2;
@@ -427,6 +434,42 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, 512);
+    if (a.npeer) {
+        // The CTA's finished output tile (its 2 TQ rows x 256 bytes of head h) to every peer of the head group:
+        // coalesced plain stores (16 threads per row), read back from this GPU's L2, while other CTAs compute.
+        const int rows = min(2 * TQ, a.Lq - q0);
+        const __half* src0 = a.out + (int64_t)b * a.sob + (int64_t)h * a.soh + (int64_t)q0 * a.sol;
+        for (int i = threadIdx.x; i < rows * 16; i += blockDim.x) {
+            const int64_t off = (int64_t)(i >> 4) * a.sol + (i & 15) * 8;
+            const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src0 + off));
+            for (int p = 0; p < a.npeer; ++p) *reinterpret_cast<uint4*>(a.peer_out[p] + (src0 - a.out) + off) = u;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            // The barrier orders every thread's peer stores before this system-scope fence; the arrivals follow it.
+            __threadfence_system();
+            for (int p = 0; p < a.npeer; ++p) atomicAdd_system(a.peer_cnt[p], 1ull);
+        }
+    }
+}
+
+// One thread waits until *cnt >= expected (acquire loads at system scope), sleeping between polls, for at most
+// timeout_ns; if the count is not reached by then it sets *err and returns, so the stream moves on and the host reads
+// the failure instead of a hung GPU.
+__global__ void wait_count_kernel(const unsigned long long* cnt, unsigned long long expected, unsigned int* err,
+                                  long long timeout_ns) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const uint64_t t0 = global_timer();
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(cnt) : "memory");
+        if (v >= expected) return;
+        if ((long long)(global_timer() - t0) > timeout_ns) {
+            atomicOr(err, 1u);
+            return;
+        }
+        __nanosleep(256);
+    }
 }
 
 // Per-row int8 quantization of Q or K rows of 128 values (hip_attention.hip:67-93, :172-194):
@@ -546,10 +589,55 @@ extern "C" int64_t b2_attention_workspace_bytes(int B, int H, int Hkv, int Lq, i
     return i8_layout(B, H, Hkv, Lq, Lk).total;
 }
 
+namespace b2 {
+namespace {
+int attention_impl(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k, int64_t skb,
+                   int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl, uint16_t* out,
+                   int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk, float scale,
+                   int int8_qk, void* workspace, int64_t workspace_bytes, uint16_t* const* peer_out,
+                   unsigned long long* const* peer_cnt, int npeer, void* stream);
+}  // namespace
+}  // namespace b2
+
 extern "C" int b2_attention(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k, int64_t skb,
                             int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl,
                             uint16_t* out, int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk,
                             float scale, int int8_qk, void* workspace, int64_t workspace_bytes, void* stream) {
+    return attention_impl(q, sqb, sqh, sql, k, skb, skh, skl, v, svb, svh, svl, out, sob, soh, sol, B, H, Hkv, Lq, Lk,
+                          scale, int8_qk, workspace, workspace_bytes, nullptr, nullptr, 0, stream);
+}
+
+extern "C" int b2_attention_gather(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k,
+                                   int64_t skb, int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh,
+                                   int64_t svl, uint16_t* out, int64_t sob, int64_t soh, int64_t sol, int B, int H,
+                                   int Hkv, int Lq, int Lk, float scale, int int8_qk, void* workspace,
+                                   int64_t workspace_bytes, uint16_t* const* peer_out,
+                                   unsigned long long* const* peer_cnt, int npeer, void* stream) {
+    if (npeer < 0 || npeer > MAX_PEERS) return fail(B2_ERR_UNSUPPORTED, "attention_gather: %d peers (at most %d)", npeer, MAX_PEERS);
+    if (npeer && (!peer_out || !peer_cnt)) return fail(B2_ERR_INVALID, "attention_gather: null peer arrays");
+    return attention_impl(q, sqb, sqh, sql, k, skb, skh, skl, v, svb, svh, svl, out, sob, soh, sol, B, H, Hkv, Lq, Lk,
+                          scale, int8_qk, workspace, workspace_bytes, peer_out, peer_cnt, npeer, stream);
+}
+
+extern "C" int b2_attention_gather_ctas(int B, int H, int Lq) {
+    if (B <= 0 || H <= 0 || Lq <= 0) return 0;
+    return ((Lq + 2 * TQ - 1) / (2 * TQ)) * B * H;
+}
+
+extern "C" int b2_wait_count(const unsigned long long* cnt, unsigned long long expected, unsigned int* err,
+                             long long timeout_ns, void* stream) {
+    if (!cnt || !err || timeout_ns <= 0) return fail(B2_ERR_INVALID, "wait_count: bad arguments");
+    wait_count_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(cnt, expected, err, timeout_ns);
+    return check_launch("wait_count_kernel");
+}
+
+namespace b2 {
+namespace {
+int attention_impl(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k, int64_t skb,
+                   int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl, uint16_t* out,
+                   int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk, float scale,
+                   int int8_qk, void* workspace, int64_t workspace_bytes, uint16_t* const* peer_out,
+                   unsigned long long* const* peer_cnt, int npeer, void* stream) {
     if (!q || !k || !v || !out) return fail(B2_ERR_INVALID, "attention: null pointer");
     if (B < 0 || H <= 0 || Hkv <= 0 || Lq < 0 || Lk <= 0 || H % Hkv)
         return fail(B2_ERR_INVALID, "attention: bad shape B=%d H=%d Hkv=%d Lq=%d Lk=%d", B, H, Hkv, Lq, Lk);
@@ -567,6 +655,13 @@ extern "C" int b2_attention(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t
     a.H = H;
     a.rep = H / Hkv;
     a.scale_log2 = scale * LOG2E;
+    for (int i = 0; i < npeer; ++i) {
+        if (!peer_out[i] || !peer_cnt[i] || !aligned16(peer_out[i]))
+            return fail(B2_ERR_INVALID, "attention_gather: peer %d buffer or counter", i);
+        a.peer_out[i] = reinterpret_cast<__half*>(peer_out[i]);
+        a.peer_cnt[i] = peer_cnt[i];
+    }
+    a.npeer = npeer;
     CUtensorMap tq, tk, tv, tks;
     const Views vq{q, sqb, sqh, sql}, vk{k, skb, skh, skl}, vv{v, svb, svh, svl};
     if (int rc = map_heads(&tv, vv, B, Hkv, Lk)) return rc;
@@ -602,3 +697,5 @@ extern "C" int b2_attention(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t
     a.qscale = qs;
     return launch_attention<true>(tq, tk, tv, tks, a, B, s);
 }
+}  // namespace
+}  // namespace b2

@@ -13,9 +13,12 @@ The reference's fused Krea-2 block (int8_gemm.py:189-226) has the same shape wit
 configuration's simplified form.
 
 Sharding (one process per GPU): the two CFG branches split first; within a branch, heads split into groups. A GPU
-computes the QKV rows and the attention of its heads, one NCCL all-gather inside the head group assembles the
-attention output (the out-proj pre-pass reads the gathered [g, T, w] buffer in place through its segment mode), and
-the out-projection and MLP run replicated inside the group. That all-gather is the only collective.
+computes the QKV rows and the attention of its heads, the head group's attention outputs are assembled on every GPU
+of the group (the out-proj pre-pass reads the gathered [g, T, w] buffer in place through its segment mode), and the
+out-projection and MLP run replicated inside the group. That exchange is the only collective. It is either an NCCL
+all-gather after the attention, or fused into the attention (FusedGather): each CTA copies its finished output tile
+into the group's peers' gathered buffers (symmetric memory) and counts its arrival there, and a stream-ordered
+bounded wait on the local counter precedes the out-projection, so the transfer overlaps the attention's compute.
 """
 import contextlib
 import dataclasses
@@ -129,12 +132,55 @@ class DiTBlock:
         del w_qkv, s_qkv
 
 
+class FusedGather:
+    """Buffers of the fused head-group gather on one rank: ``buf`` [2, g, b, T, w] fp16 (double-buffered by block
+    parity), its peers' copies at ``peer_buf`` (device addresses, one per other rank of the group, in group order),
+    an int64 arrival counter ``cnt`` and its peers' counters ``peer_cnt``, and an int32 error flag set by a wait
+    that runs out. Counters only grow: after n blocks this rank expects n * (g - 1) * (CTAs per launch) arrivals.
+
+    Reuse is safe without further synchronization: a rank writes block i + 2's tiles into a peer's buffer of parity
+    i % 2 only after its own wait for block i + 1, i.e. after every peer finished block i + 1's attention, which
+    each peer's stream orders after its block-i out-projection pre-pass, the last reader of that buffer."""
+
+    def __init__(self, buf, peer_buf, cnt, peer_cnt, err, index, timeout_ns=2_000_000_000):
+        self.buf, self.peer_buf, self.cnt, self.peer_cnt, self.err = buf, list(peer_buf), cnt, list(peer_cnt), err
+        self.index, self.timeout_ns = index, timeout_ns
+        self.blocks_done = 0
+        self.g = buf.shape[1]
+
+    @classmethod
+    def create(cls, group, group_index, g, b, T, w, device):
+        """Allocates the buffers in torch symmetric memory and exchanges their addresses inside ``group``."""
+        import torch.distributed._symmetric_memory as symm_mem
+
+        buf = symm_mem.empty((2, g, b, T, w), dtype=torch.float16, device=device)
+        cnt = symm_mem.empty((8,), dtype=torch.int64, device=device)
+        cnt.zero_()
+        torch.cuda.synchronize(device)
+        hb = symm_mem.rendezvous(buf, group.group_name)
+        hc = symm_mem.rendezvous(cnt, group.group_name)
+        peers = [p for p in range(g) if p != group_index]
+        err = torch.zeros((1,), dtype=torch.int32, device=device)
+        fg = cls(buf, [hb.buffer_ptrs[p] for p in peers], cnt, [hc.buffer_ptrs[p] for p in peers], err, group_index)
+        fg._handles = (hb, hc)  # keep the mappings alive
+        return fg
+
+    def segment(self, par):
+        """This rank's [b, T, w] segment of the parity-`par` buffer, and its byte offset."""
+        seg = self.buf[par, self.index]
+        return seg, (par * self.g + self.index) * seg.numel() * seg.element_size()
+
+    def failed(self):
+        return bool(self.err.item())
+
+
 class DiTStack:
     """Runs ``cfg.blocks`` blocks on this rank's share. ``all_gather(out, inp)`` gathers [g * n] from [n] inside the
     rank's head group (torch.distributed.all_gather_into_tensor in production)."""
 
-    def __init__(self, cfg, plan, device, seed=0, all_gather=None, timer=None):
+    def __init__(self, cfg, plan, device, seed=0, all_gather=None, timer=None, fused_gather=None):
         self.cfg, self.plan, self.device = cfg, plan, device
+        self.fused = fused_gather
         self.timer = timer or (lambda kind, work=0: contextlib.nullcontext())
         # probe(stage, *tensors), when set, sees each stage's outputs before the next stage overwrites the buffers
         # they live in (parity tests read sampled rows from them); it adds no launches when unset.
@@ -158,8 +204,10 @@ class DiTStack:
         self.act = torch.empty((M, F), dtype=torch.float16, device=dev)
         self.xa = torch.empty((M, D), dtype=torch.float16, device=dev)
 
-    def attention_part(self, blk, x):
-        """RMSNorm -> QKV of this rank's heads -> attention. x [b, T, D] fp16; returns att [b, T, hl, 128]."""
+    def attention_part(self, blk, x, gather=None):
+        """RMSNorm -> QKV of this rank's heads -> attention. x [b, T, D] fp16; returns att [b, T, hl, 128]. With
+        ``gather`` = (output [b, T, hl, 128], peer addresses, peer counters) the attention writes there and also
+        delivers each tile to the peers (ops.attention's gather)."""
         cfg, hl, t = self.cfg, self.hl, self.timer
         b, T, D = x.shape
         M = b * T
@@ -174,11 +222,13 @@ class DiTStack:
             self.probe("qkv", self.qkv)
         qkv = self.qkv.view(b, T, 3, hl, cfg.head_dim)
         q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+        att = self.att if gather is None else gather[0]
         with t("attention", 4 * b * hl * T * T * cfg.head_dim):
-            ops.attention(q, k, v, self.att.transpose(1, 2), cfg.head_dim ** -0.5)
+            ops.attention(q, k, v, att.transpose(1, 2), cfg.head_dim ** -0.5,
+                          gather=None if gather is None else gather[1:])
         if self.probe:
-            self.probe("attention", self.att)
-        return self.att
+            self.probe("attention", att)
+        return att
 
     def mlp_part(self, blk, x, att, gathered=False):
         """Out-projection (+ residual) and the SwiGLU MLP (+ residual), in place on x. ``att`` is this rank's
@@ -220,6 +270,18 @@ class DiTStack:
         return x
 
     def block(self, blk, x):
+        fg = self.fused
+        if fg is not None and self.gathered is not None:
+            par = fg.blocks_done % 2
+            seg, off = fg.segment(par)
+            b, T = x.shape[0], x.shape[1]
+            out = seg.view(b, T, self.hl, self.cfg.head_dim)
+            self.attention_part(blk, x, gather=(out, [p + off for p in fg.peer_buf], fg.peer_cnt))
+            fg.blocks_done += 1
+            expected = fg.blocks_done * (fg.g - 1) * ops.attention_gather_ctas(b, self.hl, T)
+            with self.timer("gather_wait"):
+                ops.wait_count(fg.cnt, expected, fg.err, fg.timeout_ns)
+            return self.mlp_part(blk, x, fg.buf[par], gathered=True)
         att = self.attention_part(blk, x)
         if self.gathered is not None:
             with self.timer("all_gather"):

@@ -6,6 +6,7 @@ each tensor it passes has the dtype, layout and element count the kernel will in
 anything reaches the device, and raises ``RuntimeError`` naming the tensor otherwise. These checks run before the
 CUDA-tensor check, so they hold (and are tested) without a GPU.
 """
+import ctypes
 import math
 
 import torch
@@ -308,8 +309,10 @@ def gemm_w4a4(a_q, a_scale, w_packed, w_scale, bias=None, out=None, workspace=No
 
 
 # ---------------------------------------------------------------- attention
-def attention(q, k, v, out, scale, int8_qk=False, workspace=None):
-    """Fused attention on (B, H, L, 128) fp16 views with a contiguous last dimension; writes ``out``."""
+def attention(q, k, v, out, scale, int8_qk=False, workspace=None, gather=None):
+    """Fused attention on (B, H, L, 128) fp16 views with a contiguous last dimension; writes ``out``. ``gather`` =
+    (peer output addresses, peer counter addresses) also copies each finished tile to the peers' buffers at the
+    same offsets and counts its arrival there (b2_attention_gather)."""
     for t, n in ((q, "q"), (k, "k"), (v, "v"), (out, "out")):
         if t.dim() != 4 or t.dtype != torch.float16 or t.stride(-1) != 1:
             _fail(f"attention {n} must be a 4D fp16 (B, H, L, 128) view with a contiguous last dimension")
@@ -327,10 +330,37 @@ def attention(q, k, v, out, scale, int8_qk=False, workspace=None):
     if ws_bytes and (workspace is None or not workspace.is_contiguous()
                      or workspace.numel() * workspace.element_size() < ws_bytes):
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-    call("b2_attention", ptr(q), *map(I64, q.stride()[:3]), ptr(k), *map(I64, k.stride()[:3]), ptr(v),
-         *map(I64, v.stride()[:3]), ptr(out), *map(I64, out.stride()[:3]), I(B), I(H), I(Hkv), I(Lq), I(Lk), F(scale),
-         I(int(bool(int8_qk))), ptr(workspace if ws_bytes else None), I64(ws_bytes), stream())
+    if gather is None:
+        call("b2_attention", ptr(q), *map(I64, q.stride()[:3]), ptr(k), *map(I64, k.stride()[:3]), ptr(v),
+             *map(I64, v.stride()[:3]), ptr(out), *map(I64, out.stride()[:3]), I(B), I(H), I(Hkv), I(Lq), I(Lk),
+             F(scale), I(int(bool(int8_qk))), ptr(workspace if ws_bytes else None), I64(ws_bytes), stream())
+    else:
+        peer_out, peer_cnt = gather
+        n = len(peer_out)
+        if n != len(peer_cnt) or n > 7:
+            _fail("attention gather needs one counter per peer buffer, at most 7 peers")
+        po = (ctypes.c_void_p * max(n, 1))(*[ctypes.c_void_p(int(p)) for p in peer_out])
+        pc = (ctypes.c_void_p * max(n, 1))(*[ctypes.c_void_p(int(c)) for c in peer_cnt])
+        call("b2_attention_gather", ptr(q), *map(I64, q.stride()[:3]), ptr(k), *map(I64, k.stride()[:3]), ptr(v),
+             *map(I64, v.stride()[:3]), ptr(out), *map(I64, out.stride()[:3]), I(B), I(H), I(Hkv), I(Lq), I(Lk),
+             F(scale), I(int(bool(int8_qk))), ptr(workspace if ws_bytes else None), I64(ws_bytes), po, pc, I(n),
+             stream())
     return out
+
+
+def attention_gather_ctas(B, H, Lq):
+    """Arrivals one attention_gather launch makes on each peer counter."""
+    return _lib.load().b2_attention_gather_ctas(B, H, Lq)
+
+
+def wait_count(cnt, expected, err, timeout_ns=2_000_000_000):
+    """Stream-ordered wait until the int64 counter ``cnt`` (device) reaches ``expected``; sets ``err`` (int32,
+    device) on timeout."""
+    if cnt.dtype != torch.int64 or err.dtype != torch.int32:
+        _fail("wait_count needs an int64 counter and an int32 error flag")
+    require_cuda(cnt, err)
+    call("b2_wait_count", ptr(cnt), ctypes.c_ulonglong(int(expected)), ptr(err), ctypes.c_longlong(int(timeout_ns)),
+         stream())
 
 
 # ---------------------------------------------------------------- RMSNorm

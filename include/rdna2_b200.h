@@ -151,6 +151,23 @@ int b2_attention(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const
                  int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl, uint16_t* out,
                  int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk, float scale,
                  int int8_qk, void* workspace, int64_t workspace_bytes, void* stream);
+/* b2_attention that also delivers its output to the other GPUs of a head group: the output store of
+ * hip_attention.hip attn (:363-372) plus the all-gather the sharded block needs after it, in one kernel. Each CTA,
+ * once its output tile is written to `out`, copies the tile to peer_out[p] (the same tensor offsets in peer p's
+ * buffer, which must be mapped into this GPU's address space, e.g. symmetric memory) with plain coalesced stores,
+ * fences at system scope and adds 1 to peer_cnt[p] (a 64-bit counter in peer p's memory). A launch makes
+ * b2_attention_gather_ctas(B, H, Lq) arrivals on every peer counter. npeer <= 7. */
+int b2_attention_gather(const uint16_t* q, int64_t sqb, int64_t sqh, int64_t sql, const uint16_t* k, int64_t skb,
+                        int64_t skh, int64_t skl, const uint16_t* v, int64_t svb, int64_t svh, int64_t svl,
+                        uint16_t* out, int64_t sob, int64_t soh, int64_t sol, int B, int H, int Hkv, int Lq, int Lk,
+                        float scale, int int8_qk, void* workspace, int64_t workspace_bytes, uint16_t* const* peer_out,
+                        unsigned long long* const* peer_cnt, int npeer, void* stream);
+int b2_attention_gather_ctas(int B, int H, int Lq);
+/* Stream-ordered wait for the gather: one thread polls *cnt (acquire, system scope) until it reaches `expected`;
+ * after timeout_ns without it, sets *err (nonzero) and returns so that the stream and the GPU stay usable and the
+ * host can report the failure. */
+int b2_wait_count(const unsigned long long* cnt, unsigned long long expected, unsigned int* err, long long timeout_ns,
+                  void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * RMSNorm with fp32 math, zero-centred fp32 weight: y = fp16(x * rsqrt(mean(x^2) + eps) * (w + 1)).

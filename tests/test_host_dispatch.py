@@ -227,3 +227,22 @@ def test_w4a8_forward_dispatch(pkg, calls):
           qweight_unpacked=torch.zeros((64, 256), dtype=torch.int8))
     with pytest.raises(NotImplementedError, match="scales of shape"):
         f(x, torch.zeros((64, 256), dtype=torch.uint8), torch.ones(64).half(), None, 128, torch.float16)
+
+
+def test_dit_fused_gather_dispatch(pkg, calls):
+    """Head-group mode with the fused gather: the attention delivers to the peers (b2_attention_gather), a bounded
+    stream-ordered wait on the arrival counter precedes the out-projection pre-pass, which reads the parity buffer."""
+    import importlib
+
+    dit = importlib.import_module(pkg.__name__ + ".dit")
+    cfg = dit.DiTConfig(hidden=256, heads=4, mlp=512, blocks=3, batch=2, tokens=40)
+    plan = dit.shard_plan(4, 1, cfg.batch, cfg.heads)
+    g, hl = plan.group_size, plan.head_hi - plan.head_lo
+    buf = torch.zeros((2, g, 1, cfg.tokens, hl * 128), dtype=torch.float16)
+    fg = dit.FusedGather(buf, [1 << 20], torch.zeros(8, dtype=torch.int64), [2 << 20], torch.zeros(1, dtype=torch.int32),
+                         plan.group_index)
+    stack = dit.DiTStack(cfg, plan, "cpu", fused_gather=fg)
+    stack.forward(torch.randn((1, 40, 256)).half())
+    block = ["b2_mod_quant_pack_a", "b2_gemm", "b2_attention_gather", "b2_wait_count", "b2_quant_pack_a_seg", "b2_gemm",
+             "b2_mod_quant_pack_a", "b2_gemm_swiglu", "b2_quant_pack_a", "b2_gemm"]
+    assert calls == block * cfg.blocks and fg.blocks_done == cfg.blocks
