@@ -29,6 +29,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
+DECODE_MODE, DECODE_LAYERS = "persistent", 36
 
 # DRAM traffic per launch of each workload's roofline kernel: dram__bytes_read.sum + dram__bytes_write.sum from one
 # ncu capture of that kernel on a B200 (cold L2).  Output lines still dirty in L2 when a kernel ends are not counted
@@ -39,6 +40,7 @@ NCU_TRAFFIC = {
     "w4a8": 22.17e6 + 0.60e6,        # C3, one launch
     "prepass": 40.87e6 + 0.46e6,     # C4 QKV pre-pass (MOD), one launch; the 20.4 MB int8 output stays in L2
     "decode": 15.78e6 * 19456 / 6144,  # captured on the 6144-row qkv GEMV; bytes grow with rows (2568 B per row)
+    "decode_step": None,             # per layer of decode_step_kernel (captured on a 4-layer decoder, scaled)
     "dit": 113.8e6 + 52.1e6,         # mean over the 32 W8A8 GEMM launches of one DiT step
 }
 
@@ -623,8 +625,9 @@ class DecodeC5:
         p = pkg()
         self.ops = p.ops
         decoder = importlib.import_module(p.__name__ + ".decoder")
-        self.cfg = cfg = decoder.DecoderConfig()
+        self.cfg = cfg = decoder.DecoderConfig(layers=DECODE_LAYERS)
         self.dec = decoder.TextDecoder(cfg, dev, seed=0)
+        self.dec.mode = DECODE_MODE
         self.dec.set_position(cfg.capacity - 1)
         g = torch.Generator().manual_seed(5)
         self.x_host = torch.randn((1, cfg.hidden), generator=g).pin_memory()
@@ -633,14 +636,25 @@ class DecodeC5:
         self.dec.x.copy_(self.x0)
         self.dec.capture()
         self.bytes, self.weight_bytes = self.dec.bytes_per_token()
-        self.launches_per_step = cfg.layers * decoder.TextDecoder.launches_per_layer
+        self.persistent = DECODE_MODE == "persistent"
+        self.launches_per_step = 1 if self.persistent else cfg.layers * decoder.TextDecoder.launches_per_layer
         self.events = []
-        self.config = {"workload": "C5 single-token decode", "layers": 36, "hidden": 2560, "heads": 32, "kv_heads": 8,
-                       "mlp": 9728, "kv_len": 1024, "batch": 1, "graph": "whole token step in one CUDA graph",
-                       "l2": "3.6 GB of weights per token, larger than L2"}
+        self.config = {"workload": "C5 single-token decode", "layers": cfg.layers, "hidden": 2560, "heads": 32,
+                       "kv_heads": 8, "mlp": 9728, "kv_len": 1024, "batch": 1,
+                       "mode": ("one persistent kernel per token (b2_decode_step), in a CUDA graph with its counter memset"
+                                if self.persistent else "9 launches per layer, whole token step in one CUDA graph"),
+                       "l2": f"{self.weight_bytes / 1e9:.1f} GB of weights per token, larger than L2"}
 
     def step(self, i, record=False):
         self.dec.x.copy_(self.x0)
+        if record and self.persistent:
+            # The whole step is the kernel: time the replay (the 256-byte counter memset node + decode_step_kernel).
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            self.dec.graph.replay()
+            e1.record()
+            self.events.append((e0, e1))
+            return
         if record:
             # GEMV kernel timing: the gate|up weights of every layer in turn (50 MB each, 1.8 GB together).
             L = self.dec.layers[i % len(self.dec.layers)]
@@ -665,6 +679,16 @@ class DecodeC5:
         return ms / steps
 
     def roofline(self, peaks, kms):
+        if self.dec.failed():
+            raise RuntimeError(f"decode_step reported error {self.dec.failed()}")
+        if self.persistent:
+            achieved = self.bytes / (kms * 1e-3) / 1e9
+            return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"],
+                    "traffic": (NCU_TRAFFIC["decode_step"] * self.cfg.layers if NCU_TRAFFIC["decode_step"] else None),
+                    "kernel": "decode_step_kernel<4> (the whole token: every layer's weights + the attended KV rows)",
+                    "note": (f"{peaks['source']} HBM copy bandwidth; algorithmic bytes {self.bytes / 1e9:.3f} GB per token "
+                             f"(int8 weights {self.weight_bytes / 1e9:.3f} GB + fp32 scales + KV cache rows)")}
         achieved = self.gemv_bytes / (kms * 1e-3) / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["decode"],
@@ -1051,9 +1075,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="head-group exchange of the sharded DiT stack (4 or 8 GPUs)")
+    ap.add_argument("--decode-mode", default="persistent", choices=["persistent", "layers"],
+                    help="C5: one persistent kernel per token, or 9 launches per layer")
+    ap.add_argument("--decode-layers", type=int, default=36, help="C5 layers (36; fewer only for ncu captures)")
     args = ap.parse_args()
-    global GATHER
+    global GATHER, DECODE_MODE, DECODE_LAYERS
     GATHER = args.gather
+    DECODE_MODE, DECODE_LAYERS = args.decode_mode, args.decode_layers
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":

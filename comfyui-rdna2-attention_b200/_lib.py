@@ -53,6 +53,8 @@ SIGNATURES = {
     "b2_decode_qk_rope": (I, [P, P, P, P, P, P, P, P, I, I, F, P]),
     "b2_attn_decode": (I, [P, P, P, P, P, P, P, I, I, I, I, F, P]),
     "b2_attn_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, F, P]),
+    "b2_decode_step": (I, [P, I, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, ctypes.c_longlong, P]),
+    "b2_decode_step_splits": (I, [I]),
 }
 
 _lib = None

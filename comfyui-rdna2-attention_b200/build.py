@@ -17,7 +17,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(HERE, "librdna2_b200.so")
 
-SOURCES = ["host.cpp", "prepass.cu", "gemm.cu", "gemm_w4a8.cu", "attention.cu", "norm.cu", "decode.cu"]
+SOURCES = ["host.cpp", "prepass.cu", "gemm.cu", "gemm_w4a8.cu", "attention.cu", "norm.cu", "decode.cu", "decode_step.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "-I", INCLUDE, "-I", CSRC, "-diag-suppress", "177"]

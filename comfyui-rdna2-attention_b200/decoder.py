@@ -2,14 +2,18 @@
 
 Architecture (the configuration's): hidden 2560, 36 layers, 32 query / 8 KV heads of 128, SwiGLU MLP 9728, RMSNorm,
 per-output-channel int8 linears read by the HBM-streaming GEMV, fp32 activations and fp32 decode attention over a
-fixed-capacity KV cache (int8_gemv.py:117-126). Per layer the step is 9 launches:
-  RMSNorm -> GEMV(q|k|v) -> QK-norm + rope + KV-cache write -> decode attention (split 32 + merge)
-  -> GEMV(o) with the residual in its epilogue -> RMSNorm -> GEMV(gate|up) -> GEMV(down) reading silu(gate) * up
-  as its input and adding the residual.
+fixed-capacity KV cache (int8_gemv.py:117-126). Three ways to run a token, all on this library's kernels:
+  mode "persistent" (default): the whole token, every layer, in ONE launch (b2_decode_step): one CTA per SM streams
+    its rows of every layer's weights through a shared-memory ring while grid barriers separate the stages below.
+  mode "layers": 9 launches per layer:
+    RMSNorm -> GEMV(q|k|v) -> QK-norm + rope + KV-cache write -> decode attention (split 32 + merge)
+    -> GEMV(o) with the residual in its epilogue -> RMSNorm -> GEMV(gate|up) -> GEMV(down) reading silu(gate) * up
+    as its input and adding the residual.
+  fused = False: `layer_reference`, the same layer with the element-wise work as torch ops (about 25 launches per
+    layer), kept as the reference the other two are tested against.
 The q/k/v and gate/up weights of a layer are stored concatenated, so each is one GEMV over one x. The whole step is
 captured once in a CUDA graph and replayed (the position and the cache length live on the device, as in the
-reference, int8_gemv.hip:121-131). `layer_reference` is the same layer with the element-wise work as torch ops
-(about 25 launches per layer), kept as the reference the fused layer is tested against.
+reference, int8_gemv.hip:121-131).
 """
 import dataclasses
 
@@ -83,6 +87,11 @@ class TextDecoder:
         self.qkv = torch.empty(((H + 2 * Hk) * d,), dtype=torch.float32, device=device)
         self.q = torch.empty((H, d), dtype=torch.float32, device=device)
         self.gu = torch.empty((2 * F,), dtype=torch.float32, device=device)
+        self.act = torch.empty((F,), dtype=torch.float32, device=device)
+        self.sync = torch.zeros((ops.DECODE_STEP_SYNC_WORDS,), dtype=torch.int32, device=device)
+        self.err = torch.zeros((1,), dtype=torch.int32, device=device)
+        self.table = None
+        self.mode = "persistent"
         self.fused = True
         self.graph = None
 
@@ -127,7 +136,23 @@ class TextDecoder:
         a = torch.nn.functional.silu(gu[:F]) * gu[F:]
         return x + ops.gemv_i8(a, L.w_down, L.s_down).view(1, -1)
 
+    def persistent_step(self):
+        """One token through all layers in one launch; self.x is the residual stream in and out."""
+        cfg = self.cfg
+        if self.table is None:
+            self.table = ops.decode_step_table(self.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.mlp, cfg.capacity)
+        ops.decode_step(self.table, self.x.view(-1), self.xb, self.qkv, self.att.view(-1), self.act, self.partial,
+                        self.stats, self.inv_freq, self.pos, self.lengths, self.sync, self.err, cfg.hidden, cfg.heads,
+                        cfg.kv_heads, cfg.mlp, cfg.capacity, cfg.eps)
+        return self.x
+
+    def failed(self):
+        """Error code the persistent step left (0: none; see b2_decode_step)."""
+        return int(self.err.item())
+
     def step_eager(self):
+        if self.fused and self.mode == "persistent":
+            return self.persistent_step()
         if not self.fused:
             x = self.x
             for L in self.layers:
@@ -173,4 +198,5 @@ class TextDecoder:
         kv = cfg.layers * 2 * cfg.capacity * cfg.kv_heads * cfg.head_dim * 4
         return w + s + kv, w
 
-    launches_per_layer = 9  # 2 RMSNorms, 4 GEMVs, q/k rope, decode attention (2 kernels)
+    launches_per_layer = 9  # mode "layers": 2 RMSNorms, 4 GEMVs, q/k rope, decode attention (2 kernels)
+    launches_per_token_persistent = 1  # mode "persistent": one kernel (plus the counters' memset node)

@@ -508,5 +508,77 @@ def attn_decode(q, k, v, lengths, scale, out=None, partial=None, stats=None):
     return out
 
 
+DECODE_STEP_FIELDS = ("norm_in", "norm_post", "q_norm", "k_norm", "w_qkv", "s_qkv", "w_o", "s_o", "w_gu", "s_gu",
+                      "w_down", "s_down", "k_cache", "v_cache")
+DECODE_STEP_SYNC_WORDS = 64
+
+
+def decode_step_splits(kv_heads):
+    """Position splits per kv head of decode_step on the current device."""
+    return int(_lib.load().b2_decode_step_splits(kv_heads))
+
+
+def decode_step_table(layers, hidden, heads, kv_heads, mlp, capacity):
+    """The device table of layer pointers decode_step reads: for each layer the 14 tensors of DECODE_STEP_FIELDS
+    (attributes of the layer objects), each checked for shape, dtype, contiguity and 16-byte alignment."""
+    d = HEAD_DIM
+    shapes = {
+        "norm_in": ((hidden,), torch.float32), "norm_post": ((hidden,), torch.float32),
+        "q_norm": ((d,), torch.float32), "k_norm": ((d,), torch.float32),
+        "w_qkv": (((heads + 2 * kv_heads) * d, hidden), torch.int8), "s_qkv": (((heads + 2 * kv_heads) * d,), torch.float32),
+        "w_o": ((hidden, heads * d), torch.int8), "s_o": ((hidden,), torch.float32),
+        "w_gu": ((2 * mlp, hidden), torch.int8), "s_gu": ((2 * mlp,), torch.float32),
+        "w_down": ((hidden, mlp), torch.int8), "s_down": ((hidden,), torch.float32),
+        "k_cache": (None, torch.float32), "v_cache": (None, torch.float32),
+    }
+    rows = []
+    for i, L in enumerate(layers):
+        row = []
+        for name in DECODE_STEP_FIELDS:
+            t = getattr(L, name)
+            shape, dtype = shapes[name]
+            if name.endswith("cache"):
+                if t.dtype != dtype or tuple(t.shape[-3:]) != (capacity, kv_heads, d) or t.numel() != capacity * kv_heads * d:
+                    _fail(f"decode_step layer {i} {name} must be fp32 [1, {capacity}, {kv_heads}, {d}]")
+            elif t.dtype != dtype or tuple(t.shape) != shape:
+                _fail(f"decode_step layer {i} {name} must be {dtype} {shape}, got {t.dtype} {tuple(t.shape)}")
+            if not t.is_contiguous() or t.data_ptr() % 16:
+                _fail(f"decode_step layer {i} {name} must be contiguous and 16-byte aligned")
+            row.append(t.data_ptr())
+        rows.append(row)
+    require_cuda(*(getattr(L, n) for L in layers for n in DECODE_STEP_FIELDS))
+    return torch.tensor(rows, dtype=torch.int64).to(layers[0].w_qkv.device)
+
+
+def decode_step(table, x, x2, qkv, att, act, partial, stats, inv_freq, pos, lengths, sync, err, hidden, heads, kv_heads,
+                mlp, capacity, eps, timeout_ns=2_000_000_000):
+    """One token through every layer of the table in one persistent launch (b2_decode_step). x [hidden] fp32 is
+    the residual stream in and out; the other buffers are scratch sized as the header states; sync is 64 int32
+    counters (cleared by the call), err an int32 flag the host reads after the step."""
+    d = HEAD_DIM
+    S = DECODE_SPLITS  # the kernel uses at most this many splits per kv head
+    if table.dtype != torch.int64 or table.dim() != 2 or table.shape[1] != len(DECODE_STEP_FIELDS):
+        _fail("decode_step table must be int64 [layers, 14]")
+    _vec(x, hidden, torch.float32, "decode_step x")
+    _vec(x2, hidden, torch.float32, "decode_step x2")
+    _vec(qkv, (heads + 2 * kv_heads) * d, torch.float32, "decode_step qkv")
+    _vec(att, heads * d, torch.float32, "decode_step att")
+    if act is None or act.dtype != torch.float32 or not act.is_contiguous() or act.numel() < mlp:
+        _fail("decode_step act must be contiguous fp32 with at least mlp values")
+    for t, n, k in ((partial, "partial", heads * S * d), (stats, "stats", heads * S * 2)):
+        if t is None or t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < k:
+            _fail(f"decode_step {n} must be contiguous fp32 with at least {k} values")
+    _vec(inv_freq, d // 2, torch.float32, "inv_freq")
+    if pos.dtype != torch.int64 or lengths.dtype != torch.int32:
+        _fail("decode_step needs an int64 position and int32 lengths")
+    if sync.dtype != torch.int32 or sync.numel() < DECODE_STEP_SYNC_WORDS or err.dtype != torch.int32:
+        _fail("decode_step needs int32 sync (64 words) and err")
+    require_cuda(table, x, x2, qkv, att, act, partial, stats, inv_freq, pos, lengths, sync, err)
+    call("b2_decode_step", ptr(table), I(table.shape[0]), ptr(x), ptr(x2), ptr(qkv), ptr(att), ptr(act), ptr(partial),
+         ptr(stats), ptr(inv_freq), ptr(pos), ptr(lengths), ptr(sync), ptr(err), I(hidden), I(heads), I(kv_heads),
+         I(mlp), I(capacity), F(eps), ctypes.c_longlong(int(timeout_ns)), stream())
+    return x
+
+
 def default_scale():
     return 1.0 / math.sqrt(HEAD_DIM)

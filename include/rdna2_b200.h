@@ -209,6 +209,30 @@ int b2_rms_norm_f32(const float* x, const float* w, float* y, int D, float eps, 
 int b2_decode_qk_rope(const float* qkv, const float* q_norm, const float* k_norm, const float* inv_freq,
                       const int64_t* pos, float* q_out, float* k_cache, float* v_cache, int heads, int kv_heads,
                       float eps, void* stream);
+/* One whole decode step of an int8 decoder in ONE persistent launch (one CTA per SM, cooperative): per layer
+ * RMSNorm -> q|k|v GEMV -> q/k RMSNorm + rope + cache write -> split attention + merge -> o GEMV + residual ->
+ * RMSNorm -> gate|up GEMV -> silu(gate) * up -> down GEMV + residual, with the arithmetic of gemv_i8
+ * (int8_gemv.hip:55-85) and attn_decode / attn_merge (int8_gemv.hip:124-195) around linear_forward
+ * (int8_gemv.py:48-64). It replaces the reference's per-layer sequence of those launches (and the torch ops between
+ * them) for a whole token; the stages are separated by grid barriers inside the kernel.
+ *   layers: device array of n_layers x 14 device pointers, in this order: norm_in [D], norm_post [D], q_norm [128],
+ *     k_norm [128], w_qkv int8 [(H + 2 Hk) 128, D], s_qkv [(H + 2 Hk) 128], w_o int8 [D, H 128], s_o [D],
+ *     w_gu int8 [2 F, D] (gate rows then up rows), s_gu [2 F], w_down int8 [D, F], s_down [D],
+ *     k_cache [capacity, Hk, 128], v_cache [capacity, Hk, 128] (fp32 unless stated); every one 16-byte aligned.
+ *   x [D]: the residual stream, read as the step's input and overwritten with its output. x2 [D], qkv
+ *   [(H + 2 Hk) 128], att [H 128], act [F], partial [H, S, 128], stats [H, S, 2] are scratch, S =
+ *   b2_decode_step_splits(Hk). inv_freq [64]; pos int64 [1] and lengths int32 [1] are read on the device (the
+ *   position written, and the number of cache rows attended), so a captured graph replays for any position.
+ *   sync: 64 uint32 arrival counters, cleared by this call (stream-ordered) before the launch.
+ *   err: int32 flag; nonzero after a wait ran out (1 grid barrier, 2/3 weight ring), or 4 for a position outside
+ *   the cache or a missing / misaligned table entry. A launch finding *err set does nothing.
+ * H / Hk in {1, 2, 4}; D, H 128 and F multiples of 16 and at most 10240; timeout_ns bounds every wait. */
+int b2_decode_step(const uint64_t* layers, int n_layers, float* x, float* x2, float* qkv, float* att, float* act,
+                   float* partial, float* stats, const float* inv_freq, const int64_t* pos, const int32_t* lengths,
+                   unsigned int* sync, int* err, int hidden, int heads, int kv_heads, int mlp, int capacity, float eps,
+                   long long timeout_ns, void* stream);
+/* Position splits per kv head that b2_decode_step uses on the current device (sizes partial and stats). */
+int b2_decode_step_splits(int kv_heads);
 /* fp32 split-KV decode attention + merge (int8_gemv.hip:124-180 attn_decode, :183-195 attn_merge;
  * int8_gemv.py:101-114). q [B,1,H,128], k/v [B,capacity,Hkv,128], lengths int32 [B] read on the
  * device (graph-replayable), out [B,1,H,128]. partial: fp32 [B*H, 32, 128], stats: fp32 [B*H, 32, 2]

@@ -73,3 +73,47 @@ def attn_decode(q, k, v, lengths, scale):
             p = np.exp(s)
             out[b, 0, h] = (p @ v[b, :n, h // rep]) / p.sum()
     return out
+
+
+def _rms64(x, w, eps):
+    x = np.asarray(x, np.float64)
+    return x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps) * np.asarray(w, np.float64)
+
+
+def decoder_step(x, layers, pos, length, heads, kv_heads, mlp, eps, inv_freq):
+    """One token through an int8 decoder's layers in float64: the route int8_gemv.py's decode takes around its
+    kernels, composed as the configuration-5 decoder does. Per layer
+        h = RMSNorm(x) * norm_in;  q|k|v = gemv_i8(h)                       (int8_gemv.hip:55-85, int8_gemv.py:62-63)
+        q, k = RMSNorm per head (q_norm / k_norm), half-split rotary at `pos` (angle fp32(pos * inv_freq[i]), pairs
+               (i, i + 64)); k and v written into row `pos` of the caches
+        att = softmax(q k^T / sqrt(128)) v over `length` cache rows, GQA  (int8_gemv.hip:124-195)
+        x = x + gemv_i8(att);  h = RMSNorm(x) * norm_post;  g|u = gemv_i8(h)
+        x = x + gemv_i8(silu(g) * u)
+    layers: one dict per layer holding DECODE_STEP_FIELDS' arrays (int8 weights, fp32 scales / norms, caches
+    [1, cap, kv_heads, 128]); the caches are updated in place (as float32). Returns x as float32."""
+    d = 128
+    x = np.asarray(x, np.float64).reshape(-1)
+    ang = (np.float32(pos) * np.asarray(inv_freq, F32)).astype(np.float64)
+    cos, sin = np.cos(ang), np.sin(ang)
+
+    def rope(t):
+        a, b = t[:, :64], t[:, 64:]
+        return np.concatenate((a * cos - b * sin, a * sin + b * cos), axis=1)
+
+    for L in layers:
+        h = _rms64(x, L["norm_in"], eps)
+        qkv = (np.asarray(L["w_qkv"], np.float64) @ h) * np.asarray(L["s_qkv"], np.float64)
+        q = rope(_rms64(qkv[:heads * d].reshape(heads, d), L["q_norm"], eps))
+        k = rope(_rms64(qkv[heads * d:(heads + kv_heads) * d].reshape(kv_heads, d), L["k_norm"], eps))
+        v = qkv[(heads + kv_heads) * d:].reshape(kv_heads, d)
+        kc, vc = L["k_cache"], L["v_cache"]
+        kc[0, pos] = k.astype(F32)
+        vc[0, pos] = v.astype(F32)
+        att = attn_decode(q.reshape(1, 1, heads, d), kc, vc, np.array([length]), d ** -0.5).astype(np.float64)
+        x = x + (np.asarray(L["w_o"], np.float64) @ att.reshape(-1)) * np.asarray(L["s_o"], np.float64)
+        h = _rms64(x, L["norm_post"], eps)
+        gu = (np.asarray(L["w_gu"], np.float64) @ h) * np.asarray(L["s_gu"], np.float64)
+        g, u = gu[:mlp], gu[mlp:]
+        a = g / (1.0 + np.exp(-g)) * u
+        x = x + (np.asarray(L["w_down"], np.float64) @ a) * np.asarray(L["s_down"], np.float64)
+    return x.astype(F32)

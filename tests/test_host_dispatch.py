@@ -47,12 +47,45 @@ def test_decoder_layer_is_nine_launches(pkg, calls):
     decoder = importlib.import_module(pkg.__name__ + ".decoder")
     cfg = decoder.DecoderConfig(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=128, mlp=512, capacity=16)
     dec = decoder.TextDecoder(cfg, "cpu")
+    dec.mode = "layers"
     dec.set_position(3)
     dec.step_eager()
     layer = ["b2_rms_norm_f32", "b2_gemv_i8", "b2_decode_qk_rope", "b2_attn_decode", "b2_gemv_i8_ex",
              "b2_rms_norm_f32", "b2_gemv_i8", "b2_gemv_i8_ex"]
     assert calls == layer * cfg.layers
     assert decoder.TextDecoder.launches_per_layer == len(layer) + 1  # attn_decode is two kernels (split, merge)
+
+
+def test_decoder_persistent_step_is_one_launch(pkg, calls):
+    """The default mode hands the whole token to b2_decode_step, with a table of every layer's 14 pointers."""
+    import importlib
+
+    decoder = importlib.import_module(pkg.__name__ + ".decoder")
+    cfg = decoder.DecoderConfig(hidden=256, layers=3, heads=4, kv_heads=2, head_dim=128, mlp=512, capacity=16)
+    dec = decoder.TextDecoder(cfg, "cpu")
+    assert dec.mode == "persistent"
+    for pos in (3, 4):
+        dec.set_position(pos)
+        dec.step_eager()
+    assert calls == ["b2_decode_step"] * 2
+    assert tuple(dec.table.shape) == (3, 14)
+    assert dec.table[1, 4].item() == dec.layers[1].w_qkv.data_ptr()
+    assert dec.table[2, 13].item() == dec.layers[2].v_cache.data_ptr()
+
+
+def test_decode_step_table_refuses_bad_layers(pkg):
+    import importlib
+
+    decoder = importlib.import_module(pkg.__name__ + ".decoder")
+    cfg = decoder.DecoderConfig(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=128, mlp=512, capacity=16)
+    dec = decoder.TextDecoder(cfg, "cpu")
+    dec.layers[1].s_o = dec.layers[1].s_o.double()
+    with pytest.raises(RuntimeError, match="layer 1 s_o"):
+        pkg.ops.decode_step_table(dec.layers, 256, 4, 2, 512, 16)
+    dec.layers[1].s_o = dec.layers[1].s_o.float()
+    dec.layers[0].w_gu = dec.layers[0].w_gu.t()
+    with pytest.raises(RuntimeError, match="layer 0 w_gu"):
+        pkg.ops.decode_step_table(dec.layers, 256, 4, 2, 512, 16)
 
 
 def _linear(pkg, N, K, seed):
