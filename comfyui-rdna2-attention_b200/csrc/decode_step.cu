@@ -42,14 +42,18 @@
 namespace b2 {
 namespace {
 
-constexpr int DS_CWARPS = 8;                   // consumer warps
+constexpr int DS_CWARPS = 16;                  // consumer warps (four warpgroups)
 constexpr int DS_CTHREADS = DS_CWARPS * 32;    // consumer threads (named barrier 1)
-constexpr int DS_THREADS = DS_CTHREADS + 32;   // + the producer warp
+constexpr int DS_THREADS = DS_CTHREADS + 128;  // + the producer warpgroup (one thread works)
+// Register split (setmaxnreg): launched with DS_REGS_LAUNCH per thread, the producer warpgroup gives back down to
+// DS_REGS_PRODUCER and the consumers take DS_REGS_CONSUMER: 512 * 104 + 128 * 40 = 58368 <= 640 * 96 = 61440.
+constexpr int DS_REGS_LAUNCH = 96, DS_REGS_CONSUMER = 104, DS_REGS_PRODUCER = 40;
+static_assert(DS_CTHREADS * DS_REGS_CONSUMER + 128 * DS_REGS_PRODUCER <= DS_THREADS * DS_REGS_LAUNCH, "register split");
 constexpr int DS_SLOT = 40960;                 // bytes per ring slot
 constexpr int DS_SLOTS = 4;
-constexpr int DS_INFLIGHT = 2;                 // bulk copies a producer keeps in flight (the rest of the ring holds
+constexpr int DS_INFLIGHT = 4;                 // bulk copies a producer keeps in flight (the rest of the ring holds
                                                // data that has landed); more would only queue the SM's other loads
-constexpr int DS_MAXU = 5;                     // 16-value units of the input a consumer thread holds
+constexpr int DS_MAXU = 3;                     // 16-value units of the input a consumer thread holds
 constexpr int DS_RPG = 2;                      // rows per row group per slot
 static_assert(DS_RPG == 2, "gemv_stage's finishing lanes pick v[0] / v[1]");
 constexpr int DS_HD = 128;                     // head dim
@@ -742,19 +746,47 @@ __device__ __forceinline__ bool throttle(Smem& sm, const StepArgs& a, uint32_t i
     return ring_wait(&sm.full[j % DS_SLOTS], (j / DS_SLOTS) & 1, &sm.abort, a.err, DS_ERR_EMPTY, a.timeout_ns);
 }
 
-// One lane of the producer warp: every slot of every stage of every layer, in the consumers' order.
-__device__ void producer(Smem& sm, const StepArgs& a) {
-    const int c = blockIdx.x, G = gridDim.x;
-    const uint64_t policy = l2_policy_evict_first();
-    uint32_t it = 0;
-    bool ok = true;
-    // This CTA's attention rows, prefetched into L2 while the layer's q|k|v GEMV runs.
-    const bool has_item = c < a.Hk * a.S;
-    const int g = has_item ? c / a.S : 0, s = has_item ? c % a.S : 0;
-    const int chunk = (sm.length + a.S - 1) / a.S;
-    const int s0 = min(s * chunk, sm.length), s1 = min(s0 + chunk, sm.length);
-    for (int l = 0; l < a.n_layers && ok; ++l) {
-        const uint64_t* L = a.layers + (int64_t)l * DS_FIELDS;
+// The producer's view of a layer: part 0 the q|k|v rows, 1 the attention item's K and V rows, 2 the o rows, 3 the
+// gate|up rows, 4 the down rows (GEMV stages 0, 1, 2, 3 for parts 0, 2, 3, 4).
+constexpr int DS_PARTS = 5;
+// Parts requested into L2 ahead of the part being copied into the ring. The ring holds 160 KB per SM, a few
+// microseconds of the SM's share of HBM, while attention, barriers and stage-ins leave the GEMV slots idle for about
+// twenty; requesting the rows two parts ahead (at most about 85 MB, within the 126 MB L2) keeps HBM streaming through
+// those gaps, and the ring then fills from L2.
+constexpr int DS_L2_AHEAD = 2;
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint64_t bytes) {
+    const char* b = reinterpret_cast<const char*>(p);
+    for (uint64_t o = 0; o < bytes; o += (1u << 30)) {  // pieces below 2^32 bytes
+        const uint32_t n = (uint32_t)min(bytes - o, (uint64_t)1 << 30);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + o), "r"(n) : "memory");
+    }
+}
+
+__device__ void l2_request(const StepArgs& a, int q, bool has_item, int g, int s0, int s1) {
+    const int l = q / DS_PARTS, part = q % DS_PARTS, c = blockIdx.x, G = gridDim.x;
+    if (l >= a.n_layers) return;
+    const uint64_t* L = a.layers + (int64_t)l * DS_FIELDS;
+    if (part == 1) {
+        if (!has_item) return;
+        for (int kvs = 0; kvs < 2; ++kvs) {
+            const float* cache = reinterpret_cast<const float*>(L[kvs == 0 ? F_K_CACHE : F_V_CACHE]);
+            for (int j = s0; j < s1; ++j) prefetch_l2_bulk(cache + ((int64_t)j * a.Hk + g) * DS_HD, DS_HD * 4);
+        }
+        return;
+    }
+    const int st = part == 0 ? 0 : part - 1;
+    Range r[2];
+    int K;
+    const int nr = stage_ranges(a, L, st, c, G, r, K);
+    const float* sc = scale_of(L, st);
+    for (int ri = 0; ri < nr; ++ri) {
+        if (r[ri].hi > r[ri].lo) prefetch_l2_bulk(r[ri].w + r[ri].lo * K, (uint64_t)(r[ri].hi - r[ri].lo) * K);
+        const char* b = reinterpret_cast<const char*>(sc + r[ri].lo);
+        const int64_t bytes = (r[ri].hi - r[ri].lo) * 4;
+        for (int64_t o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(b + o));
+    }
+    if (part == 0) {
         // The layer's norm weights (read by every CTA): this CTA asks for every G-th 128-byte line.
         for (int f = F_NORM_IN; f <= F_K_NORM; ++f) {
             const char* b = reinterpret_cast<const char*>(L[f]);
@@ -762,34 +794,26 @@ __device__ void producer(Smem& sm, const StepArgs& a) {
             for (int64_t o = (int64_t)c * 128; o < bytes; o += (int64_t)G * 128)
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(b + o));
         }
-        for (int st = 0; st < 4 && ok; ++st) {
-            Range r[2];
-            int K;
-            const int nr = stage_ranges(a, L, st, c, G, r, K);
-            const Geo geo = geometry(K);
-            const float* sc = scale_of(L, st);
-            for (int ri = 0; ri < nr; ++ri) {
-                const char* b = reinterpret_cast<const char*>(sc + r[ri].lo);
-                const int64_t bytes = (r[ri].hi - r[ri].lo) * 4;
-                for (int64_t o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(b + o));
-            }
-            for (int ri = 0; ri < nr && ok; ++ri) {
-                for (int64_t n = r[ri].lo; n < r[ri].hi; n += geo.rows) {
-                    const uint32_t rows = (uint32_t)min((int64_t)geo.rows, r[ri].hi - n);
-                    const int slot = it % DS_SLOTS;
-                    const uint32_t ph = (it / DS_SLOTS) & 1;
-                    if (!ring_wait(&sm.empty[slot], ph ^ 1, &sm.abort, a.err, DS_ERR_EMPTY, a.timeout_ns) ||
-                        !throttle(sm, a, it)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t bytes = rows * (uint32_t)K;
-                    mbar_arrive_expect_tx(&sm.full[slot], bytes);
-                    bulk_g2s(sm.ring[slot], r[ri].w + n * K, bytes, &sm.full[slot], policy);
-                    ++it;
-                }
-            }
-            if (st == 0 && has_item && ok) {
+    }
+}
+
+// One lane of the producer warpgroup: every slot of every stage of every layer, in the consumers' order.
+__device__ void producer(Smem& sm, const StepArgs& a) {
+    const int c = blockIdx.x, G = gridDim.x;
+    const uint64_t policy = l2_policy_evict_first();
+    uint32_t it = 0;
+    bool ok = true;
+    const bool has_item = c < a.Hk * a.S;
+    const int g = has_item ? c / a.S : 0, s = has_item ? c % a.S : 0;
+    const int chunk = (sm.length + a.S - 1) / a.S;
+    const int s0 = min(s * chunk, sm.length), s1 = min(s0 + chunk, sm.length);
+    for (int q = 0; q < DS_L2_AHEAD; ++q) l2_request(a, q, has_item, g, s0, s1);
+    for (int l = 0; l < a.n_layers && ok; ++l) {
+        const uint64_t* L = a.layers + (int64_t)l * DS_FIELDS;
+        for (int part = 0; part < DS_PARTS && ok; ++part) {
+            l2_request(a, l * DS_PARTS + part + DS_L2_AHEAD, has_item, g, s0, s1);
+            if (part == 1) {
+                if (!has_item) continue;
                 // The attention item's K rows, then its V rows, one slot each.
                 for (int kvs = 0; kvs < 2 && ok; ++kvs) {
                     const float* cache = reinterpret_cast<const float*>(L[kvs == 0 ? F_K_CACHE : F_V_CACHE]);
@@ -804,6 +828,27 @@ __device__ void producer(Smem& sm, const StepArgs& a) {
                     for (int j = s0; j < s1; ++j)
                         bulk_g2s(sm.ring[slot] + (j - s0) * DS_HD * 4, cache + ((int64_t)j * a.Hk + g) * DS_HD,
                                  DS_HD * 4, &sm.full[slot], policy);
+                    ++it;
+                }
+                continue;
+            }
+            Range r[2];
+            int K;
+            const int nr = stage_ranges(a, L, part == 0 ? 0 : part - 1, c, G, r, K);
+            const Geo geo = geometry(K);
+            for (int ri = 0; ri < nr && ok; ++ri) {
+                for (int64_t n = r[ri].lo; n < r[ri].hi; n += geo.rows) {
+                    const uint32_t rows = (uint32_t)min((int64_t)geo.rows, r[ri].hi - n);
+                    const int slot = it % DS_SLOTS;
+                    const uint32_t ph = (it / DS_SLOTS) & 1;
+                    if (!ring_wait(&sm.empty[slot], ph ^ 1, &sm.abort, a.err, DS_ERR_EMPTY, a.timeout_ns) ||
+                        !throttle(sm, a, it)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bytes = rows * (uint32_t)K;
+                    mbar_arrive_expect_tx(&sm.full[slot], bytes);
+                    bulk_g2s(sm.ring[slot], r[ri].w + n * K, bytes, &sm.full[slot], policy);
                     ++it;
                 }
             }
@@ -915,9 +960,11 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const __grid
     __syncthreads();  // nothing writes abort before every thread has read it
     if (dead) return;
     if (t >= DS_CTHREADS) {
+        regs_dec<DS_REGS_PRODUCER>();
         if (t == DS_CTHREADS) producer(sm, a);
         return;
     }
+    regs_inc<DS_REGS_CONSUMER>();
     consumers<GROUP>(sm, a);
 }
 
@@ -987,6 +1034,11 @@ extern "C" int b2_decode_step(const uint64_t* layers, int n_layers, float* x, fl
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, DS_THREADS, smem) != cudaSuccess || per_sm < 1)
         return fail(B2_ERR_CUDA, "decode_step: the kernel does not fit on an SM");
+    // The register split adds up only for the launch register count it was made for.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess || fa.numRegs != DS_REGS_LAUNCH)
+        return fail(B2_ERR_CUDA, "decode_step: kernel built with %d registers per thread, the split needs %d", fa.numRegs,
+                    DS_REGS_LAUNCH);
     cudaStream_t st = (cudaStream_t)stream;
     if (cudaMemsetAsync(sync, 0, DS_SYNC_WORDS * sizeof(unsigned), st) != cudaSuccess)
         return check_launch("decode_step: clearing the arrival counters");
