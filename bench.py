@@ -37,10 +37,10 @@ DECODE_MODE, DECODE_LAYERS = "persistent", 36
 NCU_TRAFFIC = {
     "attn": 149.87e6 + 31.14e6,      # C2 fp16, one launch
     "attn_i8": 101.35e6 + 23.09e6,   # C2 int8 QK, one launch
-    "w4a8": 22.17e6 + 0.60e6,        # C3, one launch
+    "w4a8": 36.48e6 + 6.38e6,        # C3, one launch of gemm_w4a8_wide_kernel
     "prepass": 40.87e6 + 0.46e6,     # C4 QKV pre-pass (MOD), one launch; the 20.4 MB int8 output stays in L2
     "decode": 15.78e6 * 19456 / 6144,  # captured on the 6144-row qkv GEMV; bytes grow with rows (2568 B per row)
-    "decode_step": None,             # per layer of decode_step_kernel (captured on a 4-layer decoder, scaled)
+    "decode_step": (438.05e6 + 4.04e6) / 4,  # per layer of decode_step_kernel (4-layer decoder, one launch)
     "dit": 113.8e6 + 52.1e6,         # mean over the 32 W8A8 GEMM launches of one DiT step
 }
 

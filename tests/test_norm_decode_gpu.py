@@ -192,6 +192,7 @@ def test_decoder_fused_step_matches_torch_ops(pkg, dev):
     decoder = importlib.import_module(pkg.__name__ + ".decoder")
     cfg = decoder.DecoderConfig(hidden=512, layers=3, heads=8, kv_heads=2, head_dim=128, mlp=1024, capacity=64)
     fused, ref = decoder.TextDecoder(cfg, dev, seed=1), decoder.TextDecoder(cfg, dev, seed=1)
+    fused.mode = "layers"  # the persistent mode has its own tests (test_decode_step_gpu.py)
     ref.fused = False
     x0 = torch.randn((1, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(5), device=dev)
     for dec in (fused, ref):
@@ -217,6 +218,7 @@ def test_decoder_graph_replay_matches_eager(pkg, dev):
     eager, graphed = decoder.TextDecoder(cfg, dev, seed=2), decoder.TextDecoder(cfg, dev, seed=2)
     x0 = torch.randn((1, cfg.hidden), generator=torch.Generator(device=dev).manual_seed(6), device=dev)
     for dec in (eager, graphed):
+        dec.mode = "layers"
         dec.x.copy_(x0)
         dec.set_position(20)
     eager.step_eager()
