@@ -46,8 +46,8 @@ constexpr int DS_CWARPS = 16;                  // consumer warps (four warpgroup
 constexpr int DS_CTHREADS = DS_CWARPS * 32;    // consumer threads (named barrier 1)
 constexpr int DS_THREADS = DS_CTHREADS + 128;  // + the producer warpgroup (one thread works)
 // Register split (setmaxnreg): launched with DS_REGS_LAUNCH per thread, the producer warpgroup gives back down to
-// DS_REGS_PRODUCER and the consumers take DS_REGS_CONSUMER: 512 * 104 + 128 * 40 = 58368 <= 640 * 96 = 61440.
-constexpr int DS_REGS_LAUNCH = 96, DS_REGS_CONSUMER = 104, DS_REGS_PRODUCER = 40;
+// DS_REGS_PRODUCER and the consumers take DS_REGS_CONSUMER: 512 * 104 + 128 * 56 = 60416 <= 640 * 96 = 61440.
+constexpr int DS_REGS_LAUNCH = 96, DS_REGS_CONSUMER = 104, DS_REGS_PRODUCER = 56;
 static_assert(DS_CTHREADS * DS_REGS_CONSUMER + 128 * DS_REGS_PRODUCER <= DS_THREADS * DS_REGS_LAUNCH, "register split");
 constexpr int DS_SLOT = 40960;                 // bytes per ring slot
 constexpr int DS_SLOTS = 4;
@@ -63,7 +63,9 @@ constexpr int DS_MAX_ROWS = 2 * DS_MAX_GATE;   // rows one CTA finishes in one s
 constexpr int DS_MAX_K = 10240;                // widest GEMV input, staged in shared memory
 constexpr int DS_DIGITS = 3;                   // signed int8 digits of the GEMV input (base 2^7)
 constexpr int DS_MAX_GROUP = 4;                // query heads per kv head
-constexpr int DS_SYNC_WORDS = 64;              // arrival counters cleared before each launch
+constexpr int DS_LINE = 32;                    // words per 128-byte line: one counter per line
+constexpr int DS_SYNC_WORDS = 2048;            // arrival counters (one per line) cleared before each launch
+constexpr int DS_O_ROWS = 64;                  // out-projection rows one CTA may own
 
 // Error codes written to *err.
 constexpr int DS_ERR_BARRIER = 1;  // a grid barrier ran out of time
@@ -83,14 +85,16 @@ struct StepArgs {
     float* x;        // [D] residual stream: input of layer 0, output of the last layer
     float* x2;       // [D] residual after attention
     float* qkv;      // [(H + 2 Hk) * 128]
-    float* att;      // [H * 128] merged attention output
+    float* att;      // [H * 128] floats of scratch: the merged attention output as 3 int8 digit planes of H * 128
+                     // bytes (kv group g's values at g * GW of each plane) and then one fp32 scale 2^-q per kv head
     float* act;      // [F] silu(gate) * up
     float* partial;  // [H][S][128]
     float* stats;    // [H][S][2]
     const float* inv_freq;  // [64]
     const int64_t* pos;
     const int32_t* lengths;
-    unsigned* sync;  // [0] grid barrier arrivals, [1 + g] merge arrivals of kv head g (zeroed per launch)
+    unsigned* sync;  // DS_SYNC_WORDS counters, one per 128-byte line (sync_barrier and the ones after it), all
+                     // zeroed per launch
     int* err;
     int D, H, Hk, F, cap, S;
     float eps, scale;
@@ -123,13 +127,14 @@ struct Range {
     int64_t lo, hi;  // rows
 };
 
-__device__ inline int stage_ranges(const StepArgs& a, const uint64_t* L, int st, int c, int G, Range (&r)[2], int& K) {
-    const int QKV = (a.H + 2 * a.Hk) * DS_HD;
+__device__ inline int stage_ranges(const StepArgs& a, const uint64_t* L, int st, int c, int G, Range (&r)[3], int& K) {
     switch (st) {
-        case 0:
+        case 0: {
+            const int64_t QKV = (int64_t)(a.H + 2 * a.Hk) * DS_HD;
             K = a.D;
             r[0] = {reinterpret_cast<const int8_t*>(L[F_W_QKV]), split_lo(QKV, c, G), split_lo(QKV, c + 1, G)};
             return 1;
+        }
         case 1:
             K = a.H * DS_HD;
             r[0] = {reinterpret_cast<const int8_t*>(L[F_W_O]), split_lo(a.D, c, G), split_lo(a.D, c + 1, G)};
@@ -151,6 +156,15 @@ __device__ inline int stage_ranges(const StepArgs& a, const uint64_t* L, int st,
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(DS_CTHREADS) : "memory"); }
 
 __device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, code); }
+
+// The counters, each on its own 128-byte line so that the pollers of one do not slow the others: the grid barrier's
+// arrivals; per kv head g its attention splits' arrivals and the flag that its merged output is published.
+__device__ __forceinline__ unsigned* sync_barrier(const StepArgs& a) { return a.sync; }
+__device__ __forceinline__ unsigned* sync_split(const StepArgs& a, int g) { return a.sync + DS_LINE * (1 + g); }
+__device__ __forceinline__ unsigned* sync_published(const StepArgs& a, int g) {
+    return a.sync + DS_LINE * (1 + a.Hk + g);
+}
+
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
     unsigned v;
@@ -217,6 +231,7 @@ struct Smem {
         uint32_t dig[DS_DIGITS][DS_MAX_K / 4];  // a stage's input as digit planes while it is handed out
         AttnScratch attn;                      // attention stage
         float gate[DS_MAX_GATE];               // gate rows of the gate|up stage (the input is in registers by then)
+        float opart[DS_O_ROWS][DS_CWARPS];     // out-projection: each row's partial sum per kv group
     } u;
     float row_scale[DS_MAX_ROWS], row_res[DS_MAX_ROWS];  // the stage's per-row scales and residual values
     float rope_c[DS_HD / 2], rope_s[DS_HD / 2];  // cos / sin of the position's rotary angles
@@ -319,6 +334,18 @@ __device__ __forceinline__ uint32_t digit_byte_word(float a, float b, float c, f
     return __byte_perm(lo, hi, 0x5410u);
 }
 
+// The power of two that puts max|x| = m in [32, 64): up = 2^q multiplies the values before their digits are taken,
+// inv = 2^-q undoes it on the dot products; inv is NaN when m is not finite.
+__device__ __forceinline__ void digit_scale(float m, float& up, float& inv) {
+    int q = 0;
+    if (m > 0.f && m <= 3.4e38f) {
+        const int e = (int)((__float_as_uint(m) >> 23) & 0xff) - 127;  // floor(log2 m) for normal m
+        q = min(max(5 - (e < -126 ? -127 : e), -126), 127);
+    }
+    up = ldexpf(1.f, q);
+    inv = m <= 3.4e38f ? ldexpf(1.f, -q) : __int_as_float(0x7fffffff);
+}
+
 __device__ __forceinline__ float stage_input(Smem& sm, const float* v, const float* w, float eps, const Geo& g,
                                              const Lane& l, uint4 (&xd)[DS_MAXU][DS_DIGITS]) {
     const int t = threadIdx.x, n4 = g.K / 4;
@@ -369,13 +396,8 @@ __device__ __forceinline__ float stage_input(Smem& sm, const float* v, const flo
     m = sm.pmax[0];
 #pragma unroll
     for (int i = 1; i < DS_CWARPS; ++i) m = fmaxf(m, sm.pmax[i]);
-    int q = 0;
-    if (m > 0.f && m <= 3.4e38f) {
-        const int e = (int)((__float_as_uint(m) >> 23) & 0xff) - 127;  // floor(log2 m) for normal m
-        q = min(max(5 - (e < -126 ? -127 : e), -126), 127);
-    }
-    const float up = ldexpf(1.f, q);
-    const float inv = m <= 3.4e38f ? ldexpf(1.f, -q) : __int_as_float(0x7fffffff);
+    float up, inv;
+    digit_scale(m, up, inv);
     const float M = 12582912.f;  // 1.5 * 2^23
     // Rolled loop: this code runs once per stage, and a compact body keeps it in the instruction cache.
 #pragma unroll 1
@@ -445,7 +467,7 @@ __device__ __forceinline__ bool group_all(bool p, int grp, int nthreads) {
 // K slice; with one warp per row (kw = 1) the warp finishes its rows itself, otherwise the kw warps of a row group
 // meet at their own named barrier and the group's first warp adds their partial sums. No CTA-wide barrier inside;
 // the consumers agree once at the end. Returns false (on every consumer thread alike) when a wait gave up.
-__device__ bool gemv_stage(Smem& sm, const StepArgs& a, const Range (&r)[2], int nr, const Geo& g,
+__device__ bool gemv_stage(Smem& sm, const StepArgs& a, const Range (&r)[3], int nr, const Geo& g,
                            const uint4 (&xd)[DS_MAXU][DS_DIGITS], float inv, uint32_t& it, const Fin& f) {
     const Lane l = lane_of(g);
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -500,7 +522,8 @@ __device__ bool gemv_stage(Smem& sm, const StepArgs& a, const Range (&r)[2], int
                 for (int i = 1; i < g.kw; ++i) sum = __fadd_rn(sum, sm.red[buf][l.grp * g.kw + i][lane]);
             }
             const int64_t row = n + my_row;
-            const int at = (ri == 0 ? 0 : (int)(r[0].hi - r[0].lo)) + (int)(row - r[ri].lo);  // row of the stage
+            int at = (int)(row - r[ri].lo);  // row of the stage: the ranges' rows in order
+            for (int q = 0; q < ri; ++q) at += (int)(r[q].hi - r[q].lo);
             const float y = __fmul_rn(__fmul_rn(sum, inv), sm.row_scale[at]);
             if (f.kind == FIN_STORE) {
                 f.out[row] = y;
@@ -522,10 +545,10 @@ __device__ bool gemv_stage(Smem& sm, const StepArgs& a, const Range (&r)[2], int
 __device__ bool grid_barrier(Smem& sm, const StepArgs& a, unsigned target) {
     consumer_sync();
     if (threadIdx.x == 0) {
-        red_release_add(a.sync, 1u);  // orders the CTA's writes (seen through the barrier above) before the arrival
+        red_release_add(sync_barrier(a), 1u);  // orders the CTA's writes (seen through the barrier above) first
         const uint64_t start = global_timer();
         for (uint32_t i = 0;; ++i) {
-            if (ld_acquire_u32(a.sync) >= target) break;
+            if (ld_acquire_u32(sync_barrier(a)) >= target) break;
             if ((i & 15) == 15) {
                 if (ld_volatile_i32(a.err)) {
                     sm.abort = 1;
@@ -540,6 +563,31 @@ __device__ bool grid_barrier(Smem& sm, const StepArgs& a, unsigned target) {
         }
     }
     return consumer_all(*reinterpret_cast<volatile int*>(&sm.abort) == 0);
+}
+
+// Bounded wait (one thread) until *flag reaches target; on a timeout or another CTA's failure it raises the CTA's
+// abort flag and returns false.
+__device__ bool wait_flag(Smem& sm, const StepArgs& a, const unsigned* flag, unsigned target) {
+    const uint64_t start = global_timer();
+    for (uint32_t i = 0;; ++i) {
+        if (ld_acquire_u32(flag) >= target) return true;
+        if ((i & 15) == 15) {
+            if (*reinterpret_cast<volatile int*>(&sm.abort)) return false;
+            if (ld_volatile_i32(a.err)) {
+                sm.abort = 1;
+                return false;
+            }
+            if (global_timer() - start > a.timeout_ns) {
+                set_err(a.err, DS_ERR_BARRIER);
+                sm.abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ const float* scale_of(const uint64_t* L, int st) {
+    return reinterpret_cast<const float*>(L[st == 0 ? F_S_QKV : st == 1 ? F_S_O : st == 2 ? F_S_GU : F_S_DOWN]);
 }
 
 // The attention of one layer. CTA c < Hk * S takes kv head g = c / S and positions [s0, s1) of split s = c % S.
@@ -684,7 +732,7 @@ __device__ __noinline__ bool attn_stage(Smem& sm, const StepArgs& a, const uint6
         // acq_rel: releases this CTA's partial result (ordered before by the barrier above) and, for the last
         // arrival, acquires every other split's.
         unsigned old;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + 1 + g) : "memory");
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(sync_split(a, g)) : "memory");
         sm.last = old == (unsigned)((layer + 1) * a.S - 1);
     }
     consumer_sync();
@@ -718,24 +766,118 @@ __device__ __noinline__ bool attn_stage(Smem& sm, const StepArgs& a, const uint6
         as.total[t] = total;
     }
     consumer_sync();
-#pragma unroll
-    for (int o = 0; o < OUTS; ++o) {
-        const int i = t + o * DS_CTHREADS;
-        if (i >= GROUP * DS_HD) break;
-        const int gi = i / DS_HD;
+    static_assert(OUTS == 1, "one merged value per consumer thread");
+    const bool mine = t < GROUP * DS_HD;
+    float v = 0.f;
+    if (mine) {
+        const int gi = t / DS_HD;
         float value = 0.f;
 #pragma unroll
         for (int k = 0; k < DS_MAX_SPLITS; ++k)
-            if (k < a.S) value += pv[o][k] * as.keep[gi][k];
-        const float total = as.total[gi];
-        a.att[(g * GROUP + gi) * DS_HD + i % DS_HD] = value / total;
+            if (k < a.S) value += pv[0][k] * as.keep[gi][k];
+        v = value / as.total[gi];
+    }
+    // The kv head's merged values go out as the out-projection's input: three int8 digit planes under one power of
+    // two (as stage_input forms them), then the flag that kv head g's output is published for this layer.
+    float m = mine ? (fabsf(v) <= 3.4e38f ? fabsf(v) : __int_as_float(0x7f800000)) : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) sm.pmax[w] = m;
+    consumer_sync();
+    m = sm.pmax[0];
+#pragma unroll
+    for (int i = 1; i < DS_CWARPS; ++i) m = fmaxf(m, sm.pmax[i]);
+    float up, inv;
+    digit_scale(m, up, inv);
+    const int GW = GROUP * DS_HD;
+    uint8_t* planes = reinterpret_cast<uint8_t*>(a.att);
+    float r = __fmul_rn(v, up);
+#pragma unroll
+    for (int d = 0; d < DS_DIGITS; ++d) {
+        const float M = 12582912.f;  // 1.5 * 2^23
+        const float tt = __fadd_rn(r, M);
+        r = __fmul_rn(__fsub_rn(r, __fsub_rn(tt, M)), 128.f);
+        const uint32_t b0 = __float_as_uint(tt) & 0xffu;
+        const uint32_t b1 = __shfl_down_sync(0xffffffffu, b0, 1), b2 = __shfl_down_sync(0xffffffffu, b0, 2),
+                       b3 = __shfl_down_sync(0xffffffffu, b0, 3);
+        if (mine && (t & 3) == 0)
+            *reinterpret_cast<uint32_t*>(planes + (int64_t)d * a.H * DS_HD + g * GW + t) =
+                b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+    if (t == 0) reinterpret_cast<float*>(planes + (int64_t)DS_DIGITS * a.H * DS_HD)[g] = inv;
+    consumer_sync();
+    if (t == 0) red_release_add(sync_published(a, g), 1u);
+    return true;
+}
+
+
+// The out-projection with its residual, x2 = x + W_o . att, taken kv head by kv head without a grid barrier after
+// the attention: warp w works on kv head g = w % Hk (its K slice of GROUP * 128 columns) and on every (16 / Hk)-th
+// row of each slot; it waits only for that kv head's merged output (the merging CTA's flag) and reads it as the
+// digit planes the merge published. Each (row, kv head) partial sum lands in shared memory; after the slots, the
+// CTA adds them up per row in kv-head order and finishes x2 = x + s_o * sum. The weight slots are the same as for
+// a whole-row GEMV (rows of H * 128 bytes).
+__device__ __noinline__ bool o_stage(const StepArgs& a, const uint64_t* L, int layer, uint32_t* it_io) {
+    Smem& sm = smem_struct();
+    Range r[3];
+    int K;
+    stage_ranges(a, L, 1, blockIdx.x, gridDim.x, r, K);
+    const Geo geo = geometry(K);
+    const int64_t n0 = r[0].lo;
+    const int nrows = (int)(r[0].hi - r[0].lo);
+    const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+    const float* s_o = scale_of(L, 1);
+    for (int i = t; i < nrows; i += DS_CTHREADS) {
+        sm.row_scale[i] = __ldg(s_o + n0 + i);
+        sm.row_res[i] = __ldcg(a.x + n0 + i);
+    }
+    const int GW = (a.H / a.Hk) * DS_HD, units = GW / 16, per = DS_CWARPS / a.Hk;
+    const int grp = w % a.Hk, part = w / a.Hk;
+    const uint8_t* planes = reinterpret_cast<const uint8_t*>(a.att);
+    bool ok = true;
+    if (lane == 0) ok = wait_flag(sm, a, sync_published(a, grp), (unsigned)layer + 1);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();  // the flag's acquire (lane 0) orders the whole warp's reads of the planes
+    uint4 xd[DS_DIGITS];
+    float inv = 0.f;
+    {
+        const int uc = min(lane, units - 1);
+#pragma unroll
+        for (int d = 0; d < DS_DIGITS; ++d) {
+            const uint4 dw = __ldcg(reinterpret_cast<const uint4*>(planes + (int64_t)d * a.H * DS_HD + grp * GW) + uc);
+            xd[d] = (ok && lane < units) ? dw : make_uint4(0u, 0u, 0u, 0u);
+        }
+        inv = __ldcg(reinterpret_cast<const float*>(planes + (int64_t)DS_DIGITS * a.H * DS_HD) + grp);
+    }
+    uint32_t it = *it_io;
+    for (int64_t n = n0; n < n0 + nrows && ok; n += geo.rows) {
+        const int rows = (int)min((int64_t)geo.rows, n0 + nrows - n);
+        const int slot = it % DS_SLOTS;
+        const uint32_t ph = (it / DS_SLOTS) & 1;
+        ++it;
+        ok = ring_wait(&sm.full[slot], ph, &sm.abort, a.err, DS_ERR_FULL, a.timeout_ns);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const uint8_t* base = sm.ring[slot] + grp * GW + min(lane, units - 1) * 16;
+        for (int rr = part; rr < rows; rr += per) {
+            int acc[DS_DIGITS] = {};
+            dot_unit(lds128(base + rr * K), xd, acc);
+            const float y = __fmul_rn(warp_sum(combine_digits(acc)), inv);
+            if (lane == 0) sm.u.opart[(int)(n - n0) + rr][grp] = y;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    }
+    *it_io = it;
+    if (!consumer_all(ok)) return false;
+    for (int i = t; i < nrows; i += DS_CTHREADS) {
+        float sum = sm.u.opart[i][0];
+        for (int gg = 1; gg < a.Hk; ++gg) sum = __fadd_rn(sum, sm.u.opart[i][gg]);
+        a.x2[n0 + i] = __fadd_rn(sm.row_res[i], __fmul_rn(sum, sm.row_scale[i]));
     }
     return true;
 }
 
-__device__ __forceinline__ const float* scale_of(const uint64_t* L, int st) {
-    return reinterpret_cast<const float*>(L[st == 0 ? F_S_QKV : st == 1 ? F_S_O : st == 2 ? F_S_GU : F_S_DOWN]);
-}
 
 // Before the producer issues slot `it`: slot it - DS_INFLIGHT has landed. At about 45 GB/s per SM and a microsecond
 // of latency, two 40 KB copies in flight keep the SM's share of HBM busy; every further byte in flight would only
@@ -776,7 +918,7 @@ __device__ void l2_request(const StepArgs& a, int q, bool has_item, int g, int s
         return;
     }
     const int st = part == 0 ? 0 : part - 1;
-    Range r[2];
+    Range r[3];
     int K;
     const int nr = stage_ranges(a, L, st, c, G, r, K);
     const float* sc = scale_of(L, st);
@@ -832,7 +974,7 @@ __device__ void producer(Smem& sm, const StepArgs& a) {
                 }
                 continue;
             }
-            Range r[2];
+            Range r[3];
             int K;
             const int nr = stage_ranges(a, L, part == 0 ? 0 : part - 1, c, G, r, K);
             const Geo geo = geometry(K);
@@ -862,16 +1004,16 @@ __device__ void producer(Smem& sm, const StepArgs& a) {
     }
 }
 
-// One GEMV stage of a layer (0 q|k|v, 1 o, 2 gate|up, 3 down): its input formed, then the CTA's rows. One copy of
+// One GEMV stage of a layer (0 q|k|v, 2 gate|up, 3 down; the o rows are o_stage's): its input formed, then the CTA's rows. One copy of
 // this code serves all four stages (it is not inlined), which keeps the kernel's instruction footprint small: the
 // code outside the slot loop runs once per stage and is fetched again each time.
 __device__ __noinline__ bool layer_gemv(const StepArgs& a, const uint64_t* L, int st, uint32_t* it_io) {
     Smem& sm = smem_struct();
-    Range r[2];
+    Range r[3];
     int K;
     const int nr = stage_ranges(a, L, st, blockIdx.x, gridDim.x, r, K);
     const Geo g = geometry(K);
-    const float* src = st == 0 ? a.x : st == 1 ? a.att : st == 2 ? a.x2 : a.act;
+    const float* src = st == 0 ? a.x : st == 2 ? a.x2 : a.act;
     const float* nw = reinterpret_cast<const float*>(st == 0 ? L[F_NORM_IN] : st == 2 ? L[F_NORM_POST] : 0);
     Fin f;
     f.scale = scale_of(L, st);
@@ -880,14 +1022,12 @@ __device__ __noinline__ bool layer_gemv(const StepArgs& a, const uint64_t* L, in
     f.residual = st == 1 ? a.x : st == 3 ? a.x2 : nullptr;
     // The scales (and residual values) of every row the CTA finishes in this stage, into shared memory, in the same
     // round trip as the stage's input; stage_input's barriers publish them.
-    {
-        const int n0 = (int)(r[0].hi - r[0].lo), nrows = n0 + (nr > 1 ? (int)(r[1].hi - r[1].lo) : 0);
-        for (int i = threadIdx.x; i < nrows; i += DS_CTHREADS) {
-            const int64_t row = i < n0 ? r[0].lo + i : r[1].lo + (i - n0);
-            sm.row_scale[i] = __ldg(f.scale + row);
-            if (f.residual) sm.row_res[i] = __ldcg(f.residual + row);
+    for (int ri = 0, at0 = 0; ri < nr; at0 += (int)(r[ri].hi - r[ri].lo), ++ri)
+        for (int i = threadIdx.x; i < (int)(r[ri].hi - r[ri].lo); i += DS_CTHREADS) {
+            sm.row_scale[at0 + i] = __ldg(f.scale + r[ri].lo + i);
+            if (f.residual) sm.row_res[at0 + i] = __ldcg(f.residual + r[ri].lo + i);
         }
-    }
+    if (nr == 0) return true;  // no rows here (fewer rows than SMs)
     uint4 xd[DS_MAXU][DS_DIGITS];
     const float inv = stage_input(sm, src, nw, a.eps, g, lane_of(g), xd);
     f.kind = st == 0 ? FIN_STORE : st == 2 ? FIN_GATE_UP : FIN_RESIDUAL;
@@ -915,9 +1055,9 @@ __device__ void consumers(Smem& sm, const StepArgs& a) {
         // q|k|v = W_qkv . rms(x) * norm_in
         if (!layer_gemv(a, L, 0, &it) || !grid_barrier(sm, a, ++nb * G)) return;
         // attention -> att
-        if (!attn_stage<GROUP>(sm, a, L, l, &it) || !grid_barrier(sm, a, ++nb * G)) return;
-        // x2 = x + W_o . att
-        if (!layer_gemv(a, L, 1, &it) || !grid_barrier(sm, a, ++nb * G)) return;
+        if (!attn_stage<GROUP>(sm, a, L, l, &it)) return;
+        // x2 = x + W_o . att, kv head by kv head as their merged outputs appear (no grid barrier before it)
+        if (!o_stage(a, L, l, &it) || !grid_barrier(sm, a, ++nb * G)) return;
         // act = silu(gate) * up of W_gu . rms(x2) * norm_post
         if (!layer_gemv(a, L, 2, &it) || !grid_barrier(sm, a, ++nb * G)) return;
         // x = x2 + W_down . act
@@ -982,10 +1122,12 @@ extern "C" int b2_decode_step(const uint64_t* layers, int n_layers, float* x, fl
         timeout_ns <= 0)
         return fail(B2_ERR_INVALID, "decode_step: bad arguments");
     if (heads % kv_heads) return fail(B2_ERR_INVALID, "decode_step: heads %d not a multiple of kv_heads %d", heads, kv_heads);
+    if (kv_heads > DS_CWARPS || DS_CWARPS % kv_heads)
+        return fail(B2_ERR_UNSUPPORTED, "decode_step: %d kv heads (1, 2, 4, 8 or 16)", kv_heads);
     const int group = heads / kv_heads;
     if (group != 1 && group != 2 && group != 4)
         return fail(B2_ERR_UNSUPPORTED, "decode_step: %d query heads per kv head (1, 2 or 4)", group);
-    if (kv_heads > DS_SYNC_WORDS - 1) return fail(B2_ERR_UNSUPPORTED, "decode_step: more than %d kv heads", DS_SYNC_WORDS - 1);
+    if (DS_LINE * (1 + 2 * kv_heads) > DS_SYNC_WORDS) return fail(B2_ERR_UNSUPPORTED, "decode_step: too many kv heads");
     const int Ks[3] = {hidden, heads * DS_HD, mlp};
     for (int K : Ks) {
         if (K % 16) return fail(B2_ERR_UNSUPPORTED, "decode_step: GEMV width %d is not a multiple of 16", K);
@@ -999,6 +1141,8 @@ extern "C" int b2_decode_step(const uint64_t* layers, int n_layers, float* x, fl
     const int S = std::min(DS_MAX_SPLITS, G / kv_heads);
     if (S < 1) return fail(B2_ERR_UNSUPPORTED, "decode_step: %d kv heads on %d SMs", kv_heads, G);
     if ((mlp + G - 1) / G > DS_MAX_GATE) return fail(B2_ERR_UNSUPPORTED, "decode_step: MLP width %d too large", mlp);
+    if ((hidden + G - 1) / G > DS_O_ROWS)
+        return fail(B2_ERR_UNSUPPORTED, "decode_step: hidden %d gives more than %d output rows per SM", hidden, DS_O_ROWS);
     if (((heads + 2 * kv_heads) * DS_HD + G - 1) / G > DS_MAX_ROWS || (hidden + G - 1) / G > DS_MAX_ROWS)
         return fail(B2_ERR_UNSUPPORTED, "decode_step: more than %d rows per SM in one GEMV", DS_MAX_ROWS);
     if ((capacity + S - 1) / S * DS_HD * 4 > DS_SLOT)

@@ -510,7 +510,7 @@ def attn_decode(q, k, v, lengths, scale, out=None, partial=None, stats=None):
 
 DECODE_STEP_FIELDS = ("norm_in", "norm_post", "q_norm", "k_norm", "w_qkv", "s_qkv", "w_o", "s_o", "w_gu", "s_gu",
                       "w_down", "s_down", "k_cache", "v_cache")
-DECODE_STEP_SYNC_WORDS = 64
+DECODE_STEP_SYNC_WORDS = 2048
 
 
 def decode_step_splits(kv_heads):
@@ -553,7 +553,7 @@ def decode_step_table(layers, hidden, heads, kv_heads, mlp, capacity):
 def decode_step(table, x, x2, qkv, att, act, partial, stats, inv_freq, pos, lengths, sync, err, hidden, heads, kv_heads,
                 mlp, capacity, eps, timeout_ns=2_000_000_000):
     """One token through every layer of the table in one persistent launch (b2_decode_step). x [hidden] fp32 is
-    the residual stream in and out; the other buffers are scratch sized as the header states; sync is 64 int32
+    the residual stream in and out; the other buffers are scratch sized as the header states; sync is 2048 int32
     counters (cleared by the call), err an int32 flag the host reads after the step."""
     d = HEAD_DIM
     S = DECODE_SPLITS  # the kernel uses at most this many splits per kv head
@@ -572,7 +572,7 @@ def decode_step(table, x, x2, qkv, att, act, partial, stats, inv_freq, pos, leng
     if pos.dtype != torch.int64 or lengths.dtype != torch.int32:
         _fail("decode_step needs an int64 position and int32 lengths")
     if sync.dtype != torch.int32 or sync.numel() < DECODE_STEP_SYNC_WORDS or err.dtype != torch.int32:
-        _fail("decode_step needs int32 sync (64 words) and err")
+        _fail(f"decode_step needs int32 sync ({DECODE_STEP_SYNC_WORDS} words) and err")
     require_cuda(table, x, x2, qkv, att, act, partial, stats, inv_freq, pos, lengths, sync, err)
     call("b2_decode_step", ptr(table), I(table.shape[0]), ptr(x), ptr(x2), ptr(qkv), ptr(att), ptr(act), ptr(partial),
          ptr(stats), ptr(inv_freq), ptr(pos), ptr(lengths), ptr(sync), ptr(err), I(hidden), I(heads), I(kv_heads),

@@ -214,19 +214,21 @@ int b2_decode_qk_rope(const float* qkv, const float* q_norm, const float* k_norm
  * RMSNorm -> gate|up GEMV -> silu(gate) * up -> down GEMV + residual, with the arithmetic of gemv_i8
  * (int8_gemv.hip:55-85) and attn_decode / attn_merge (int8_gemv.hip:124-195) around linear_forward
  * (int8_gemv.py:48-64). It replaces the reference's per-layer sequence of those launches (and the torch ops between
- * them) for a whole token; the stages are separated by grid barriers inside the kernel.
+ * them) for a whole token; the stages are separated by grid barriers inside the kernel, except the out-projection,
+ * which takes each kv head's slice of its input as soon as that kv head's attention is merged.
  *   layers: device array of n_layers x 14 device pointers, in this order: norm_in [D], norm_post [D], q_norm [128],
  *     k_norm [128], w_qkv int8 [(H + 2 Hk) 128, D], s_qkv [(H + 2 Hk) 128], w_o int8 [D, H 128], s_o [D],
  *     w_gu int8 [2 F, D] (gate rows then up rows), s_gu [2 F], w_down int8 [D, F], s_down [D],
  *     k_cache [capacity, Hk, 128], v_cache [capacity, Hk, 128] (fp32 unless stated); every one 16-byte aligned.
  *   x [D]: the residual stream, read as the step's input and overwritten with its output. x2 [D], qkv
- *   [(H + 2 Hk) 128], att [H 128], act [F], partial [H, S, 128], stats [H, S, 2] are scratch, S =
- *   b2_decode_step_splits(Hk). inv_freq [64]; pos int64 [1] and lengths int32 [1] are read on the device (the
+ *   [(H + 2 Hk) 128], att [H 128] (it holds the merged attention output as int8 digit planes and scales), act [F],
+ *   partial [H, S, 128], stats [H, S, 2] are scratch, S = b2_decode_step_splits(Hk). inv_freq [64]; pos int64 [1] and lengths int32 [1] are read on the device (the
  *   position written, and the number of cache rows attended), so a captured graph replays for any position.
- *   sync: 64 uint32 arrival counters, cleared by this call (stream-ordered) before the launch.
+ *   sync: 2048 uint32 (8 KB) of arrival counters, cleared by this call (stream-ordered) before the launch.
  *   err: int32 flag; nonzero after a wait ran out (1 grid barrier, 2/3 weight ring), or 4 for a position outside
  *   the cache or a missing / misaligned table entry. A launch finding *err set does nothing.
- * H / Hk in {1, 2, 4}; D, H 128 and F multiples of 16 and at most 10240; timeout_ns bounds every wait. */
+ * H / Hk in {1, 2, 4}; Hk in {1, 2, 4, 8, 16}; D, H 128 and F multiples of 16 and at most 10240; at most 64 output
+ * rows of D per SM; timeout_ns bounds every wait. */
 int b2_decode_step(const uint64_t* layers, int n_layers, float* x, float* x2, float* qkv, float* att, float* act,
                    float* partial, float* stats, const float* inv_freq, const int64_t* pos, const int32_t* lengths,
                    unsigned int* sync, int* err, int hidden, int heads, int kv_heads, int mlp, int capacity, float eps,
