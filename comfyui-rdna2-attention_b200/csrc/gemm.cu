@@ -5,12 +5,14 @@
 //   y = (float)acc * as[m] * ws[n] (+ (float)bias[n]) -> fp16
 //   residual: out = fp16(R[m,n] + fp16(G[m / L, n] * y))
 //
-// Structure: a persistent kernel, one CTA per SM, 6 warps; tiles 128 x BN (BN = 128, 192 or 256, whichever needs the
+// Structure: a persistent kernel, one CTA per SM, 10 warps; tiles 128 x BN (BN = 128, 192 or 256, whichever needs the
 // fewest waves x width) or, for large problems, 256 x 256 on CTA pairs (gemm_w8a8_pair_kernel below).
 //   warp 0      TMA producer: 128x128 A tiles and BNx128 B tiles (128-byte swizzle) into a STAGES-deep ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=BN, K=32 per instruction)
-//   warps 2..5  epilogue: tcgen05.ld of the int32 accumulator (each warp its 32-lane quarter), dequant,
-//               bias, residual, fp16 through a swizzled shared-memory box and one TMA store per 32 x 32 box
+//   warps 2..9  epilogue: tcgen05.ld of the int32 accumulator (two warps per 32-lane quarter, alternate 16-column
+//               boxes), dequant, bias, residual, fp16 through a swizzled shared-memory box and one TMA store per
+//               32 x 16 box. One warp per quarter left the epilogue latency-bound (a 128-row tile's 192 columns took
+//               5 us on one wave); two warps per scheduler overlap each other's waits.
 // Two TMEM accumulators (BN columns each) let the epilogue of tile i overlap the main loop of tile i+1.
 #include "common.cuh"
 #include "host.hpp"
@@ -22,13 +24,14 @@ __device__ unsigned int g_status;
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes = int8 values per k-block (one 128-byte swizzle atom)
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 320;
+constexpr int EPI_WARPS = 8;  // warps 2..9
 
-// Epilogue staging: per epilogue warp EPI_BUFS boxes of 32 rows x 64 bytes (32 fp16 columns).
+// Epilogue staging: per epilogue warp EPI_BUFS boxes of 32 rows x 32 bytes (16 fp16 columns).
 constexpr int EPI_BUFS = 3;
-constexpr int EPI_BUF_BYTES = 32 * 64;
+constexpr int EPI_BUF_BYTES = 32 * 32;
 constexpr int EPI_WARP_BYTES = EPI_BUFS * EPI_BUF_BYTES;
-constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
+constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
 
 template <int BN>
 struct Cfg {
@@ -39,7 +42,7 @@ struct Cfg {
     static constexpr int ACC_STRIDE = BN == 192 ? 256 : BN;  // TMEM columns between the two accumulators
     static constexpr int TMEM_COLS = 2 * ACC_STRIDE;          // allocations are powers of two
     static constexpr int BAR_BYTES = 512;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + BN * 8 + 1024;
 };
 
 struct GemmArgs {
@@ -67,13 +70,14 @@ __device__ __forceinline__ void epilogue_chunk_i32(const GemmArgs& g, uint32_t t
             *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
 }
 
-// One epilogue warp's share of a tile: 32 accumulator rows (TMEM lanes of the warp's quarter) x ncols columns,
-// 32 columns at a time. Row `lane` of the chunk is dequantized in registers and written into a staging box with the
-// 64-byte swizzle (16-byte piece j of row r at piece j ^ ((r >> 1) & 3): the row-per-lane writes are free of bank
-// conflicts), and lane 0 stores the 32 x 32 box with one TMA store, so the output leaves in whole lines (TMA clips
-// rows >= M and columns >= N). With a residual, lane 0 brings the matching box of R in by TMA one chunk ahead into
-// the next box. The warp's n-th chunk uses box n % 3; a box is refilled only after the store that last read it is
-// done reading (bulk_wait_read), and every R load is waited for before the function returns.
+// One epilogue warp's share of a tile: 32 accumulator rows (TMEM lanes of the warp's quarter) x the tile's 16-column
+// boxes half, half + 2, ... (the two warps of a quarter take alternate boxes). Row `lane` of a box is dequantized in
+// registers and written into a staging box of 32 rows x 32 bytes with the 32-byte swizzle (16-byte piece j of row r
+// at piece j ^ ((r >> 2) & 1): the row-per-lane writes are free of bank conflicts), and lane 0 stores the box with
+// one TMA store (TMA clips rows >= M and columns >= N). With a residual, lane 0 brings the warp's next box of R in by
+// TMA one box ahead into the next staging box. The warp's n-th box uses staging box n % 3; a staging box is refilled
+// only after the store that last read it is done reading (bulk_wait_read), and every R load is waited for before the
+// function returns.
 struct EpiCtx {
     unsigned char* buf;  // EPI_BUFS boxes
     uint64_t* rbar;      // EPI_BUFS barriers for the residual loads
@@ -96,58 +100,79 @@ __device__ __noinline__ void epi_drain(EpiCtx& e) {
     e.inflight = 0;
 }
 
-// Per-column scale, bias and (per row) gate of 32 columns. Columns past N are clamped to the last group of 8 (N % 8
-// == 0); their results are never stored.
+// The tile's per-column weight scales and bias (as fp32), staged in shared memory by the 128 epilogue threads
+// (t = 0..127) while the k-loop still runs: no chunk of the epilogue waits on an L2 round trip for them, and the
+// bias is converted once per tile instead of once per row. Columns past N are clamped to the last group of 4 or 8
+// (N % 8 == 0); their results are never stored.
+template <int BN>
+__device__ __forceinline__ void epi_stage_cols(const GemmArgs& g, float* cw, float* cb, int n0, int t) {
+    if (!g.ws) return;  // raw int32 output: no epilogue parameters
+    if (t < BN / 4) {
+        reinterpret_cast<float4*>(cw)[t] = __ldg(reinterpret_cast<const float4*>(g.ws + min(n0 + 4 * t, g.N - 4)));
+    } else if (t < BN / 4 + BN / 8) {
+        const int i = t - BN / 4;
+        const uint4 h = g.bias ? __ldg(reinterpret_cast<const uint4*>(g.bias + min(n0 + 8 * i, g.N - 8)))
+                               : make_uint4(0, 0, 0, 0);
+        const float2 f0 = upk2(h2_to_f2(h.x)), f1 = upk2(h2_to_f2(h.y)), f2 = upk2(h2_to_f2(h.z)),
+                     f3 = upk2(h2_to_f2(h.w));
+        reinterpret_cast<float4*>(cb)[2 * i] = make_float4(f0.x, f0.y, f1.x, f1.y);
+        reinterpret_cast<float4*>(cb)[2 * i + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+    }
+}
+
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// The per-row gate of 16 columns from global memory (columns past N clamped to the last group of 8, their results
+// never stored).
 struct EpiParams {
-    float4 w[8];
-    uint4 b[4];
-    uint4 gt[4];
+    uint4 gt[2];
 };
 
 __device__ __forceinline__ void epi_params(const GemmArgs& g, const __half* gate_row, int nb, EpiParams& p) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int col = min(nb + 8 * j, g.N - 8);
-        p.w[2 * j] = __ldg(reinterpret_cast<const float4*>(g.ws + col));
-        p.w[2 * j + 1] = __ldg(reinterpret_cast<const float4*>(g.ws + col) + 1);
-        p.b[j] = g.bias ? __ldg(reinterpret_cast<const uint4*>(g.bias + col)) : make_uint4(0, 0, 0, 0);
-        p.gt[j] = gate_row ? __ldg(reinterpret_cast<const uint4*>(gate_row + col)) : make_uint4(0, 0, 0, 0);
-    }
+    for (int j = 0; j < 2; ++j)
+        p.gt[j] = gate_row ? __ldg(reinterpret_cast<const uint4*>(gate_row + min(nb + 8 * j, g.N - 8)))
+                           : make_uint4(0, 0, 0, 0);
 }
 
-// The dequant of one chunk runs on fp32 pairs: v = fp32(acc) * as * ws (two roundings, as the scalar form), + bias,
+// The dequant of one box runs on fp32 pairs: v = fp32(acc) * as * ws (two roundings, as the scalar form), + bias,
 // then fp16; the residual fp16(R + fp16(G * y)) uses fp16 pair operations, which round exactly like the fp32 form
 // (fp32 holds the exact sum or product of two fp16 values to within a rounding that cannot move the fp16 result).
-// The parameters of chunk c + 1 load while chunk c computes.
-template <int NCH>
+// The gate of the warp's next box loads while this one computes; sa is the row's activation scale, read before the
+// accumulator was ready. NB = 16-column boxes in a full tile.
+template <int NB>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorMap* tmC, const CUtensorMap* tmR,
-                                              EpiCtx& e, uint32_t taddr, int row0, int n0, volatile int* abort) {
+                                              EpiCtx& e, uint32_t taddr, int row0, int n0, int half, const float* cw,
+                                              const float* cb, float sa, volatile int* abort) {
     const int lane = threadIdx.x & 31;
     const int m = row0 + lane;
     const bool row_ok = m < g.M;
-    const uint64_t sa2 = splat2(row_ok ? g.as[m] : 0.f);
-    const int nc = min(NCH, (g.N - n0 + 31) / 32);
+    const uint64_t sa2 = splat2(sa);
+    const int nc = min(NB, (g.N - n0 + 15) / 16);
     const bool res = g.R != nullptr;
     const __half* gate_row = (res && row_ok) ? g.G + (int64_t)(m / g.L) * g.N : nullptr;
-    const int sw = (lane >> 1) & 3;
+    const int sw = (lane >> 2) & 1;
     bool ok = true;
     EpiParams P[2];
-    epi_params(g, gate_row, n0, P[0]);
-    if (res && lane == 0) {
+    epi_params(g, gate_row, n0 + 16 * half, P[0]);
+    if (res && lane == 0 && half < nc) {
         bulk_wait_read<EPI_BUFS - 1>();
-        epi_load_r(tmR, e, e.n, n0, row0);
+        epi_load_r(tmR, e, e.n, n0 + 16 * half, row0);
     }
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
+    for (int i = 0; i < NB / 2; ++i) {
+        const int c = 2 * i + half;
         if (c >= nc) break;
-        EpiParams& p = P[c & 1];
-        if (c + 1 < nc) epi_params(g, gate_row, n0 + 32 * (c + 1), P[(c + 1) & 1]);
+        EpiParams& p = P[i & 1];
+        if (c + 2 < nc) epi_params(g, gate_row, n0 + 16 * (c + 2), P[(i + 1) & 1]);
         const uint32_t b = e.n % EPI_BUFS;
         unsigned char* box = e.buf + b * EPI_BUF_BYTES;
         if (res) {
-            if (lane == 0 && c + 1 < nc) {
+            if (lane == 0 && c + 2 < nc) {
                 bulk_wait_read<EPI_BUFS - 2>();
-                epi_load_r(tmR, e, e.n + 1, n0 + 32 * (c + 1), row0);
+                epi_load_r(tmR, e, e.n + 1, n0 + 16 * (c + 2), row0);
             }
             if (!mbar_wait(&e.rbar[b], (e.n / EPI_BUFS) & 1, abort, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
                 ok = false;
@@ -158,13 +183,16 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
             if (lane == 0) bulk_wait_read<EPI_BUFS - 1>();
             __syncwarp();
         }
-        uint32_t r[32];
-        tmem_ld32_wait(taddr + 32 * c, r);
-        unsigned char* row = box + lane * 64;
+        uint32_t r[16];
+        tmem_ld16_wait(taddr + 16 * c, r);
+        unsigned char* row = box + lane * 32;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float* wv = reinterpret_cast<const float*>(&p.w[2 * j]);
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&p.b[j]);
+        for (int j = 0; j < 2; ++j) {
+            float wv[8], bv[8];
+            *reinterpret_cast<float4*>(wv) = *reinterpret_cast<const float4*>(cw + 16 * c + 8 * j);
+            *reinterpret_cast<float4*>(wv + 4) = *reinterpret_cast<const float4*>(cw + 16 * c + 8 * j + 4);
+            *reinterpret_cast<float4*>(bv) = *reinterpret_cast<const float4*>(cb + 16 * c + 8 * j);
+            *reinterpret_cast<float4*>(bv + 4) = *reinterpret_cast<const float4*>(cb + 16 * c + 8 * j + 4);
             const uint32_t* gw = reinterpret_cast<const uint32_t*>(&p.gt[j]);
             uint4* slot = reinterpret_cast<uint4*>(row + ((j ^ sw) << 4));
             uint4 rr = make_uint4(0, 0, 0, 0);
@@ -179,8 +207,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
                 if (g.bias) {
                     // Scalar adds: a packed add after the packed multiply was fused into one rounding by the
                     // compiler, which moved some results by an fp16 step.
-                    const float2 f = upk2(v), bf = upk2(h2_to_f2(bw[q]));
-                    v = pk2(__fadd_rn(f.x, bf.x), __fadd_rn(f.y, bf.y));
+                    const float2 f = upk2(v);
+                    v = pk2(__fadd_rn(f.x, bv[2 * q]), __fadd_rn(f.y, bv[2 * q + 1]));
                 }
                 uint32_t y = f2_to_h2(v);
                 if (res) y = h2_as_u32(__hadd2_rn(u32_as_h2(rw[q]), __hmul2_rn(u32_as_h2(gw[q]), u32_as_h2(y))));
@@ -191,7 +219,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            tma_store_2d(tmC, box, n0 + 32 * c, row0);
+            tma_store_2d(tmC, box, n0 + 16 * c, row0);
             bulk_commit();
         }
         ++e.n;
@@ -201,52 +229,44 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
 }
 
 // SwiGLU epilogue of a 256-wide tile whose weight rows hold gate features [f, f + 128) in columns 0..127 and the
-// matching up features in columns 128..255 (rows interleaved in blocks of 128). Output chunk oc (32 features) pairs
-// accumulator columns 32 oc (gate) and 128 + 32 oc (up): g and u are the epilogue's fp16 values, then
-// fp16(fp16(g sigmoid(g)) u) with the same arithmetic as the pre-pass's SwiGLU, written as one 32 x 32 box of
-// C[M, N/2] at feature column n0 / 2 + 32 oc. A chunk's per-column scales load while its TMEM columns are read.
-struct SwiParams {
-    float4 wg[8], wu[8];
-};
-
-__device__ __forceinline__ void swi_params(const GemmArgs& g, int n0, int oc, SwiParams& p) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        p.wg[j] = __ldg(reinterpret_cast<const float4*>(g.ws + n0 + 32 * oc) + j);
-        p.wu[j] = __ldg(reinterpret_cast<const float4*>(g.ws + n0 + 128 + 32 * oc) + j);
-    }
-}
-
+// matching up features in columns 128..255 (rows interleaved in blocks of 128). Output box ob (16 features) pairs
+// accumulator columns 16 ob (gate) and 128 + 16 ob (up): g and u are the epilogue's fp16 values, then
+// fp16(fp16(g sigmoid(g)) u) with the same arithmetic as the pre-pass's SwiGLU, written as one 32 x 16 box of
+// C[M, N/2] at feature column n0 / 2 + 16 ob; the two warps of a quarter take alternate boxes. The per-column scales
+// come from the tile's staged columns.
 __device__ __forceinline__ void epilogue_tile_swiglu(const GemmArgs& g, const CUtensorMap* tmC, EpiCtx& e,
-                                                     uint32_t taddr, int row0, int n0) {
+                                                     uint32_t taddr, int row0, int n0, int half, const float* cw,
+                                                     float sa) {
     const int lane = threadIdx.x & 31;
-    const int m = row0 + lane;
-    const uint64_t sa2 = splat2(m < g.M ? g.as[m] : 0.f);
-    const int sw = (lane >> 1) & 3;
+    const uint64_t sa2 = splat2(sa);
+    const int sw = (lane >> 2) & 1;
 #pragma unroll
-    for (int oc = 0; oc < 4; ++oc) {
-        SwiParams p;
-        swi_params(g, n0, oc, p);
+    for (int i = 0; i < 4; ++i) {
+        const int ob = 2 * i + half;
+        float wg[16], wu[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            *reinterpret_cast<float4*>(wg + 4 * j) = reinterpret_cast<const float4*>(cw + 16 * ob)[j];
+            *reinterpret_cast<float4*>(wu + 4 * j) = reinterpret_cast<const float4*>(cw + 128 + 16 * ob)[j];
+        }
         unsigned char* box = e.buf + (e.n % EPI_BUFS) * EPI_BUF_BYTES;
         if (lane == 0) bulk_wait_read<EPI_BUFS - 1>();
         __syncwarp();
-        uint32_t rg[32], ru[32];
-        tmem_ld32_wait(taddr + 32 * oc, rg);
-        tmem_ld32_wait(taddr + 128 + 32 * oc, ru);
-        const float* wg = reinterpret_cast<const float*>(p.wg);
-        const float* wu = reinterpret_cast<const float*>(p.wu);
-        unsigned char* row = box + lane * 64;
+        uint32_t rg[16], ru[16];
+        tmem_ld16_wait(taddr + 16 * ob, rg);
+        tmem_ld16_wait(taddr + 128 + 16 * ob, ru);
+        unsigned char* row = box + lane * 32;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 2; ++j) {
             uint4 o;
             uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const int i = 8 * j + 2 * q;
-                const uint32_t gh = f2_to_h2(mul2(mul2(pk2((float)(int32_t)rg[i], (float)(int32_t)rg[i + 1]), sa2),
-                                                  pk2(wg[i], wg[i + 1])));
-                const uint32_t uh = f2_to_h2(mul2(mul2(pk2((float)(int32_t)ru[i], (float)(int32_t)ru[i + 1]), sa2),
-                                                  pk2(wu[i], wu[i + 1])));
+                const int k = 8 * j + 2 * q;
+                const uint32_t gh = f2_to_h2(mul2(mul2(pk2((float)(int32_t)rg[k], (float)(int32_t)rg[k + 1]), sa2),
+                                                  pk2(wg[k], wg[k + 1])));
+                const uint32_t uh = f2_to_h2(mul2(mul2(pk2((float)(int32_t)ru[k], (float)(int32_t)ru[k + 1]), sa2),
+                                                  pk2(wu[k], wu[k + 1])));
                 ow[q] = swiglu_h2(gh, uh);
             }
             *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) = o;
@@ -254,7 +274,7 @@ __device__ __forceinline__ void epilogue_tile_swiglu(const GemmArgs& g, const CU
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            tma_store_2d(tmC, box, n0 / 2 + 32 * oc, row0);
+            tma_store_2d(tmC, box, n0 / 2 + 16 * ob, row0);
             bulk_commit();
         }
         ++e.n;
@@ -275,8 +295,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* tfull = bars + 2 * C_::STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint64_t* rbars = drain + 1;  // [4][EPI_BUFS]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 4 * EPI_BUFS);
+    uint64_t* rbars = drain + 1;  // [EPI_WARPS][EPI_BUFS]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + EPI_WARPS * EPI_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -291,10 +311,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], 32 * EPI_WARPS);
         }
         mbar_init(drain, 1);
-        for (int i = 0; i < 4 * EPI_BUFS; ++i) mbar_init(&rbars[i], 1);
+        for (int i = 0; i < EPI_WARPS * EPI_BUFS; ++i) mbar_init(&rbars[i], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -389,31 +409,43 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
         }
     } else {
-        const int quarter = warp & 3;
+        const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
         const int row_local = quarter * 32 + lane;
-        EpiCtx e{staging + quarter * EPI_WARP_BYTES, rbars + quarter * EPI_BUFS, 0u, 0u};
+        EpiCtx e{staging + ew * EPI_WARP_BYTES, rbars + ew * EPI_BUFS, 0u, 0u};
+        float* cw = reinterpret_cast<float*>(staging + EPI_BYTES + C_::BAR_BYTES);
+        float* cb = cw + BN;
+        bool ok = true;
         int it = 0;
+        // Every epilogue thread passes both named barriers of every tile, after a failed wait too, so that none is
+        // left waiting at one.
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
-            tc_fence_after();
             const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+            named_bar_sync(1, 32 * EPI_WARPS);  // the epilogue warps are done with the previous tile's columns
+            if (ok) epi_stage_cols<BN>(g, cw, cb, n0, threadIdx.x - 64);
+            named_bar_sync(1, 32 * EPI_WARPS);
+            if (!ok) continue;
+            const float sa = (g.as && m0 + row_local < g.M) ? g.as[m0 + row_local] : 0.f;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                ok = false;
+                continue;
+            }
+            tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * C_::ACC_STRIDE;
-            bool ok = true;
             if (g.C32) {
                 const int m = m0 + row_local;
                 const bool row_ok = m < g.M;
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+                for (int c = half; c < BN / 32; c += 2) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
             } else if (BN == 256 && g.swiglu) {
-                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + quarter * 32, n0);
+                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + quarter * 32, n0, half, cw, sa);
             } else {
-                ok = epilogue_tile<BN / 32>(g, &tmC, &tmR, e, taddr, m0 + quarter * 32, n0, abort_flag);
+                ok = epilogue_tile<BN / 16>(g, &tmC, &tmR, e, taddr, m0 + quarter * 32, n0, half, cw, cb, sa,
+                                            abort_flag);
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
-            if (!ok) break;
         }
         if (lane == 0) bulk_wait<0>();
     }
@@ -435,7 +467,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 constexpr int PAIR_STAGES = 6;
 constexpr int PAIR_HALF = 128 * BK;                    // 16 KB: 128 rows x 128 bytes
 constexpr int PAIR_STAGE_BYTES = 2 * PAIR_HALF;        // A half + B half
-constexpr int PAIR_SMEM = PAIR_STAGES * PAIR_STAGE_BYTES + EPI_BYTES + 512 + 1024;
+constexpr int PAIR_SMEM = PAIR_STAGES * PAIR_STAGE_BYTES + EPI_BYTES + 512 + 256 * 8 + 1024;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -450,8 +482,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     uint64_t* tfull = bars + 2 * PAIR_STAGES;   // [2] (each CTA)
     uint64_t* tempty = tfull + 2;               // [2] (CTA 0)
     uint64_t* drain = tempty + 2;
-    uint64_t* rbars = drain + 1;                // [4][EPI_BUFS] (each CTA)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + 4 * EPI_BUFS);
+    uint64_t* rbars = drain + 1;                // [EPI_WARPS][EPI_BUFS] (each CTA)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbars + EPI_WARPS * EPI_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -468,10 +500,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 8);  // one arrival per epilogue warp of each CTA
+            mbar_init(&tempty[a], 2 * EPI_WARPS);  // one arrival per epilogue warp of each CTA
         }
         mbar_init(drain, 1);
-        for (int i = 0; i < 4 * EPI_BUFS; ++i) mbar_init(&rbars[i], 1);
+        for (int i = 0; i < EPI_WARPS * EPI_BUFS; ++i) mbar_init(&rbars[i], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -563,33 +595,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
         }
     } else {
-        const int quarter = warp & 3;
+        const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
         const int row_local = quarter * 32 + lane;
         const uint32_t tempty0 = map_to_rank(smem_u32(tempty), 0);
-        EpiCtx e{staging + quarter * EPI_WARP_BYTES, rbars + quarter * EPI_BUFS, 0u, 0u};
+        EpiCtx e{staging + ew * EPI_WARP_BYTES, rbars + ew * EPI_BUFS, 0u, 0u};
+        float* cw = reinterpret_cast<float*>(staging + EPI_BYTES + 512);
+        float* cb = cw + 256;
+        bool ok = true;
         int it = 0;
+        // Every epilogue thread passes both named barriers of every tile, after a failed wait too.
         for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) break;
-            tc_fence_after();
             const int m0 = (tile % num_m) * 256, n0 = (tile / num_m) * 256;
+            named_bar_sync(1, 32 * EPI_WARPS);  // the epilogue warps are done with the previous tile's columns
+            if (ok) epi_stage_cols<256>(g, cw, cb, n0, threadIdx.x - 64);
+            named_bar_sync(1, 32 * EPI_WARPS);
+            if (!ok) continue;
+            const int mrow = m0 + 128 * rank + row_local;
+            const float sa = (g.as && mrow < g.M) ? g.as[mrow] : 0.f;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
+                ok = false;
+                continue;
+            }
+            tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * 256;
-            bool ok = true;
             if (g.C32) {
                 const int m = m0 + 128 * rank + row_local;
                 const bool row_ok = m < g.M;
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+                for (int c = half; c < 8; c += 2) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
             } else if (g.swiglu) {
-                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + 128 * rank + quarter * 32, n0);
+                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + 128 * rank + quarter * 32, n0, half, cw, sa);
             } else {
-                ok = epilogue_tile<8>(g, &tmC, &tmR, e, taddr, m0 + 128 * rank + quarter * 32, n0, abort_flag);
+                ok = epilogue_tile<16>(g, &tmC, &tmR, e, taddr, m0 + 128 * rank + quarter * 32, n0, half, cw, cb, sa,
+                                       abort_flag);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tempty0 + acc * 8);
-            if (!ok) break;
         }
         if (lane == 0) bulk_wait<0>();
     }
@@ -601,19 +645,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
-// Output (and residual) maps: fp16 [M, N] row-major, 32 x 32 boxes with the 64-byte swizzle of the staging boxes.
+// Output (and residual) maps: fp16 [M, N] row-major, 16-column x 32-row boxes with the 32-byte swizzle of the staging
+// boxes.
 // The raw int32 path stores from registers and gets the A map as a placeholder.
 int make_out_maps(const GemmArgs& g, const CUtensorMap& fallback, CUtensorMap* tc, CUtensorMap* tr) {
     *tc = fallback;
     *tr = fallback;
     if (g.C32) return B2_OK;
     const int nc = g.swiglu ? g.N / 2 : g.N;
-    if (int rc = make_map_2d(tc, g.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, nc, g.M, (uint64_t)nc * 2, 32, 32,
-                             CU_TENSOR_MAP_SWIZZLE_64B))
+    if (int rc = make_map_2d(tc, g.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, nc, g.M, (uint64_t)nc * 2, 16, 32,
+                             CU_TENSOR_MAP_SWIZZLE_32B))
         return rc;
     if (g.R)
-        if (int rc = make_map_2d(tr, g.R, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.N, g.M, (uint64_t)g.N * 2, 32, 32,
-                                 CU_TENSOR_MAP_SWIZZLE_64B))
+        if (int rc = make_map_2d(tr, g.R, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.N, g.M, (uint64_t)g.N * 2, 16, 32,
+                                 CU_TENSOR_MAP_SWIZZLE_32B))
             return rc;
     return B2_OK;
 }
