@@ -330,6 +330,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the operands may come from the kernel launched before this one
 
     if (warp == 0) {
         if (lane == 0) {
@@ -520,6 +521,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     cluster_sync();  // both CTAs' barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the operands may come from the kernel launched before this one
 
     if (warp == 0) {
         if (lane == 0) {
@@ -645,6 +647,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
+// Launches a GEMM kernel with programmatic stream serialization: its CTAs may start (barrier set-up, TMEM
+// allocation, descriptor prefetch) while the previous kernel of the stream finishes, and wait in pdl_wait() for its
+// results.
+template <class Kern>
+int launch_pdl(Kern kernel, dim3 grid, int smem, cudaStream_t stream, const char* name, const CUtensorMap& ta,
+               const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tr, const GemmArgs& g) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, tr, g);
+    if (e != cudaSuccess) return fail(B2_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+    return check_launch(name);
+}
+
 // Output (and residual) maps: fp16 [M, N] row-major, 16-column x 32-row boxes with the 32-byte swizzle of the staging
 // boxes.
 // The raw int32 path stores from registers and gets the A map as a placeholder.
@@ -686,8 +709,7 @@ int launch_pair(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_
     }
     const int tiles = ((g.M + 255) / 256) * ((g.N + 255) / 256);
     const int nc = tiles < clusters[dev] ? tiles : clusters[dev];
-    gemm_w8a8_pair_kernel<<<2 * nc, GEMM_THREADS, PAIR_SMEM, stream>>>(ta, tb, tc, tr, g);
-    return check_launch("gemm_w8a8_pair_kernel");
+    return launch_pdl(gemm_w8a8_pair_kernel, dim3(2 * nc), PAIR_SMEM, stream, "gemm_w8a8_pair_kernel", ta, tb, tc, tr, g);
 }
 
 template <int BN>
@@ -705,8 +727,7 @@ int launch_bn(const int8_t* A, const int8_t* B, const GemmArgs& g, cudaStream_t 
     }
     const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_w8a8_kernel<BN><<<grid, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(ta, tb, tc, tr, g);
-    return check_launch("gemm_w8a8_kernel");
+    return launch_pdl(gemm_w8a8_kernel<BN>, dim3(grid), Cfg<BN>::SMEM, stream, "gemm_w8a8_kernel", ta, tb, tc, tr, g);
 }
 
 int run(const int8_t* A, const int8_t* B, GemmArgs& g, cudaStream_t stream) {

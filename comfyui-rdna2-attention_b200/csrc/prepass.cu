@@ -262,6 +262,7 @@ template <int ACT>
 __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ float red[2][R128_MAX_WARPS];
+    pdl_trigger();  // a GEMM launched after this kernel may run its set-up meanwhile; it waits for the data
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nwarps = blockDim.x >> 5;
     const int K = a.K;
@@ -490,6 +491,7 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
 template <int ACT, int ROT, bool I4 = false>
 __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const PrepassArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
+    pdl_trigger();  // a GEMM launched after this kernel may run its set-up meanwhile; it waits for the data
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * PP_WARPS + warp;
     if (row >= a.M) return;
