@@ -5,14 +5,15 @@
 //   y = (float)acc * as[m] * ws[n] (+ (float)bias[n]) -> fp16
 //   residual: out = fp16(R[m,n] + fp16(G[m / L, n] * y))
 //
-// Structure: a persistent kernel, one CTA per SM, 10 warps; tiles 128 x BN (BN = 128, 192 or 256, whichever needs the
+// Structure: a persistent kernel, one CTA per SM, 14 warps; tiles 128 x BN (BN = 128, 192 or 256, whichever needs the
 // fewest waves x width) or, for large problems, 256 x 256 on CTA pairs (gemm_w8a8_pair_kernel below).
 //   warp 0      TMA producer: 128x128 A tiles and BNx128 B tiles (128-byte swizzle) into a STAGES-deep ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=BN, K=32 per instruction)
-//   warps 2..9  epilogue: tcgen05.ld of the int32 accumulator (two warps per 32-lane quarter, alternate 16-column
-//               boxes), dequant, bias, residual, fp16 through a swizzled shared-memory box and one TMA store per
-//               32 x 16 box. One warp per quarter left the epilogue latency-bound (a 128-row tile's 192 columns took
-//               5 us on one wave); two warps per scheduler overlap each other's waits.
+//   warps 2..13 epilogue: tcgen05.ld of the int32 accumulator (three warps per 32-lane quarter, every third
+//               16-column box), dequant, bias, residual, fp16 through a swizzled shared-memory box and one TMA store
+//               per 32 x 16 box. One warp per quarter left the epilogue latency-bound (a 128-row tile's 192 columns
+//               took 5 us on one wave, 3.4 us with two warps per quarter); more warps per scheduler overlap each
+//               other's waits.
 // Two TMEM accumulators (BN columns each) let the epilogue of tile i overlap the main loop of tile i+1.
 #include "common.cuh"
 #include "host.hpp"
@@ -24,11 +25,12 @@ __device__ unsigned int g_status;
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes = int8 values per k-block (one 128-byte swizzle atom)
-constexpr int GEMM_THREADS = 320;
-constexpr int EPI_WARPS = 8;  // warps 2..9
+constexpr int EPI_WARPS = 12;  // warps 2..13
+constexpr int EPI_SPLIT = EPI_WARPS / 4;  // epilogue warps per TMEM lane quarter
+constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
 
 // Epilogue staging: per epilogue warp EPI_BUFS boxes of 32 rows x 32 bytes (16 fp16 columns).
-constexpr int EPI_BUFS = 3;
+constexpr int EPI_BUFS = 2;
 constexpr int EPI_BUF_BYTES = 32 * 32;
 constexpr int EPI_WARP_BYTES = EPI_BUFS * EPI_BUF_BYTES;
 constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
@@ -71,11 +73,11 @@ __device__ __forceinline__ void epilogue_chunk_i32(const GemmArgs& g, uint32_t t
 }
 
 // One epilogue warp's share of a tile: 32 accumulator rows (TMEM lanes of the warp's quarter) x the tile's 16-column
-// boxes half, half + 2, ... (the two warps of a quarter take alternate boxes). Row `lane` of a box is dequantized in
+// boxes part, part + EPI_SPLIT, ... (the EPI_SPLIT warps of a quarter take turns). Row `lane` of a box is dequantized in
 // registers and written into a staging box of 32 rows x 32 bytes with the 32-byte swizzle (16-byte piece j of row r
 // at piece j ^ ((r >> 2) & 1): the row-per-lane writes are free of bank conflicts), and lane 0 stores the box with
 // one TMA store (TMA clips rows >= M and columns >= N). With a residual, lane 0 brings the warp's next box of R in by
-// TMA one box ahead into the next staging box. The warp's n-th box uses staging box n % 3; a staging box is refilled
+// TMA one box ahead into the other staging box. The warp's n-th box uses staging box n % 2; a staging box is refilled
 // only after the store that last read it is done reading (bulk_wait_read), and every R load is waited for before the
 // function returns.
 struct EpiCtx {
@@ -144,7 +146,7 @@ __device__ __forceinline__ void epi_params(const GemmArgs& g, const __half* gate
 // accumulator was ready. NB = 16-column boxes in a full tile.
 template <int NB>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorMap* tmC, const CUtensorMap* tmR,
-                                              EpiCtx& e, uint32_t taddr, int row0, int n0, int half, const float* cw,
+                                              EpiCtx& e, uint32_t taddr, int row0, int n0, int part, const float* cw,
                                               const float* cb, float sa, volatile int* abort) {
     const int lane = threadIdx.x & 31;
     const int m = row0 + lane;
@@ -156,23 +158,23 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
     const int sw = (lane >> 2) & 1;
     bool ok = true;
     EpiParams P[2];
-    epi_params(g, gate_row, n0 + 16 * half, P[0]);
-    if (res && lane == 0 && half < nc) {
+    epi_params(g, gate_row, n0 + 16 * part, P[0]);
+    if (res && lane == 0 && part < nc) {
         bulk_wait_read<EPI_BUFS - 1>();
-        epi_load_r(tmR, e, e.n, n0 + 16 * half, row0);
+        epi_load_r(tmR, e, e.n, n0 + 16 * part, row0);
     }
 #pragma unroll
-    for (int i = 0; i < NB / 2; ++i) {
-        const int c = 2 * i + half;
+    for (int i = 0; i < (NB + EPI_SPLIT - 1) / EPI_SPLIT; ++i) {
+        const int c = EPI_SPLIT * i + part;
         if (c >= nc) break;
         EpiParams& p = P[i & 1];
-        if (c + 2 < nc) epi_params(g, gate_row, n0 + 16 * (c + 2), P[(i + 1) & 1]);
+        if (c + EPI_SPLIT < nc) epi_params(g, gate_row, n0 + 16 * (c + EPI_SPLIT), P[(i + 1) & 1]);
         const uint32_t b = e.n % EPI_BUFS;
         unsigned char* box = e.buf + b * EPI_BUF_BYTES;
         if (res) {
-            if (lane == 0 && c + 2 < nc) {
+            if (lane == 0 && c + EPI_SPLIT < nc) {
                 bulk_wait_read<EPI_BUFS - 2>();
-                epi_load_r(tmR, e, e.n + 1, n0 + 16 * (c + 2), row0);
+                epi_load_r(tmR, e, e.n + 1, n0 + 16 * (c + EPI_SPLIT), row0);
             }
             if (!mbar_wait(&e.rbar[b], (e.n / EPI_BUFS) & 1, abort, &g_status, B2_DEV_TIMEOUT_EPILOGUE)) {
                 ok = false;
@@ -232,17 +234,18 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
 // matching up features in columns 128..255 (rows interleaved in blocks of 128). Output box ob (16 features) pairs
 // accumulator columns 16 ob (gate) and 128 + 16 ob (up): g and u are the epilogue's fp16 values, then
 // fp16(fp16(g sigmoid(g)) u) with the same arithmetic as the pre-pass's SwiGLU, written as one 32 x 16 box of
-// C[M, N/2] at feature column n0 / 2 + 16 ob; the two warps of a quarter take alternate boxes. The per-column scales
+// C[M, N/2] at feature column n0 / 2 + 16 ob; the EPI_SPLIT warps of a quarter take turns. The per-column scales
 // come from the tile's staged columns.
 __device__ __forceinline__ void epilogue_tile_swiglu(const GemmArgs& g, const CUtensorMap* tmC, EpiCtx& e,
-                                                     uint32_t taddr, int row0, int n0, int half, const float* cw,
+                                                     uint32_t taddr, int row0, int n0, int part, const float* cw,
                                                      float sa) {
     const int lane = threadIdx.x & 31;
     const uint64_t sa2 = splat2(sa);
     const int sw = (lane >> 2) & 1;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int ob = 2 * i + half;
+    for (int i = 0; i < (8 + EPI_SPLIT - 1) / EPI_SPLIT; ++i) {
+        const int ob = EPI_SPLIT * i + part;
+        if (ob >= 8) break;
         float wg[16], wu[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
         }
     } else {
-        const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
+        const int ew = warp - 2, quarter = warp & 3, part = ew >> 2;  // part: the warp's turn within its quarter
         const int row_local = quarter * 32 + lane;
         EpiCtx e{staging + ew * EPI_WARP_BYTES, rbars + ew * EPI_BUFS, 0u, 0u};
         float* cw = reinterpret_cast<float*>(staging + EPI_BYTES + C_::BAR_BYTES);
@@ -438,11 +441,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 const int m = m0 + row_local;
                 const bool row_ok = m < g.M;
 #pragma unroll 1
-                for (int c = half; c < BN / 32; c += 2) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+                for (int c = part; c < BN / 32; c += EPI_SPLIT) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
             } else if (BN == 256 && g.swiglu) {
-                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + quarter * 32, n0, half, cw, sa);
+                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + quarter * 32, n0, part, cw, sa);
             } else {
-                ok = epilogue_tile<BN / 16>(g, &tmC, &tmR, e, taddr, m0 + quarter * 32, n0, half, cw, cb, sa,
+                ok = epilogue_tile<BN / 16>(g, &tmC, &tmR, e, taddr, m0 + quarter * 32, n0, part, cw, cb, sa,
                                             abort_flag);
             }
             tc_fence_before();
@@ -597,7 +600,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait_drain(drain, 0, 100000000ull)) atomicOr(&g_status, B2_DEV_TIMEOUT_DRAIN);
         }
     } else {
-        const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
+        const int ew = warp - 2, quarter = warp & 3, part = ew >> 2;  // part: the warp's turn within its quarter
         const int row_local = quarter * 32 + lane;
         const uint32_t tempty0 = map_to_rank(smem_u32(tempty), 0);
         EpiCtx e{staging + ew * EPI_WARP_BYTES, rbars + ew * EPI_BUFS, 0u, 0u};
@@ -626,11 +629,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
                 const int m = m0 + 128 * rank + row_local;
                 const bool row_ok = m < g.M;
 #pragma unroll 1
-                for (int c = half; c < 8; c += 2) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
+                for (int c = part; c < 8; c += EPI_SPLIT) epilogue_chunk_i32(g, taddr + c * 32, m, row_ok, n0 + c * 32);
             } else if (g.swiglu) {
-                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + 128 * rank + quarter * 32, n0, half, cw, sa);
+                epilogue_tile_swiglu(g, &tmC, e, taddr, m0 + 128 * rank + quarter * 32, n0, part, cw, sa);
             } else {
-                ok = epilogue_tile<16>(g, &tmC, &tmR, e, taddr, m0 + 128 * rank + quarter * 32, n0, half, cw, cb, sa,
+                ok = epilogue_tile<16>(g, &tmC, &tmR, e, taddr, m0 + 128 * rank + quarter * 32, n0, part, cw, cb, sa,
                                        abort_flag);
             }
             tc_fence_before();
