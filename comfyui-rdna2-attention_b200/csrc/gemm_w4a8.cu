@@ -138,6 +138,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W4_THREADS, 1)
     cluster_sync();  // both CTAs' barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // the operands may come from the kernel launched before this one
 
     if (warp == 0) {
         regs_dec<REGS_CTRL>();
@@ -413,6 +414,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(WIDE_THREADS, 1)
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // the operands may come from the kernel launched before this one
 
     if (warp < 4) {
         regs_dec<WIDE_REGS_CTRL>();
@@ -592,6 +594,26 @@ unsigned int read_status_gemm_w4a8() {
 
 using namespace b2;
 
+// Launches a W4A8 kernel with programmatic stream serialization: its CTAs may set up while the pre-pass that made
+// its activations finishes, and read them after pdl_wait().
+template <class Kern>
+int launch_pdl(Kern kernel, int grid, int threads, int smem, void* stream, const char* name, const CUtensorMap& ta,
+               const CUtensorMap& tw, const CUtensorMap& ts, const W4Args& g) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tw, ts, g);
+    if (e != cudaSuccess) return fail(B2_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+    return check_launch(name);
+}
+
 extern "C" int b2_gemm_w4a8(const int8_t* A, const uint8_t* Wp, const float* as, const float* gscale, const uint16_t* bias,
                             uint16_t* C, int M, int N, int K, void* stream) {
     if (!A || !Wp || !as || !gscale || !C) return fail(B2_ERR_INVALID, "gemm_w4a8: null pointer");
@@ -637,8 +659,7 @@ extern "C" int b2_gemm_w4a8(const int8_t* A, const uint8_t* Wp, const float* as,
     W4Args g{as, gscale, reinterpret_cast<const __half*>(bias), reinterpret_cast<__half*>(C), M, N, K};
     const int tiles = ((M + 255) / 256) * ((N + TN - 1) / TN);
     const int nc = tiles < clusters[dev] ? tiles : clusters[dev];
-    gemm_w4a8_pair_kernel<<<2 * nc, W4_THREADS, SMEM, (cudaStream_t)stream>>>(ta, tw, ts, g);
-    return check_launch("gemm_w4a8_pair_kernel");
+    return launch_pdl(gemm_w4a8_pair_kernel, 2 * nc, W4_THREADS, SMEM, stream, "gemm_w4a8_pair_kernel", ta, tw, ts, g);
 }
 
 extern "C" int b2_gemm_w4a8_wide(const int8_t* A, const int8_t* W, const float* as, const float* gscale,
@@ -684,8 +705,8 @@ extern "C" int b2_gemm_w4a8_wide(const int8_t* A, const int8_t* W, const float* 
     W4Args g{as, gscale, reinterpret_cast<const __half*>(bias), reinterpret_cast<__half*>(C), M, N, K};
     const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
     const int nc = tiles < clusters[dev] ? tiles : clusters[dev];
-    gemm_w4a8_wide_kernel<<<2 * nc, WIDE_THREADS, WIDE_SMEM, (cudaStream_t)stream>>>(ta, tw, ts, g);
-    return check_launch("gemm_w4a8_wide_kernel");
+    return launch_pdl(gemm_w4a8_wide_kernel, 2 * nc, WIDE_THREADS, WIDE_SMEM, stream, "gemm_w4a8_wide_kernel", ta, tw, ts,
+                      g);
 }
 
 // ---------------------------------------------------------------- per-channel W4A4
