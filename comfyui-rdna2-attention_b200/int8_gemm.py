@@ -136,16 +136,26 @@ def w4a4_ineligible(x, qweight, wscales, bias, convrot_groupsize, compute_dtype,
 def wrap_w4a4(original):
     """convrot_w4a4_forward of the Int4 loader on the sm_100a kernels (int8_gemm.py:90-103): ConvRot-256 and
     int4-valued per-token activations in one pre-pass, the packed weight widened to int8 and multiplied on the
-    tcgen05 int8 GEMM with int32 accumulation, the per-channel epilogue. Ineligible calls raise (no fallback)."""
+    tcgen05 int8 GEMM with int32 accumulation, the per-channel epilogue. ``qweight_unpacked``, the weight widened to
+    int8 [N, K] once at load time (as w4a8_forward takes it), feeds the GEMM directly; without it the packed weight
+    is widened per call into a temporary, as the reference re-packs it (int8_gemm.py:73-75). Both give the same result
+    bit for bit. Ineligible calls raise (no fallback)."""
     def convrot_w4a4_forward(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation=False,
                              qweight_unpacked=None, x_rot=None, orig_shape=None):
         reason = w4a4_ineligible(x, qweight, wscales, bias, convrot_groupsize, compute_dtype, skip_rotation, x_rot)
         if reason:
             raise NotImplementedError(f"convrot_w4a4_forward: {reason}")
         N, K = qweight.shape[0], qweight.shape[1] * 2
+        if qweight_unpacked is not None and (qweight_unpacked.dtype != torch.int8
+                                             or tuple(qweight_unpacked.shape) != (N, K)):
+            raise NotImplementedError(f"convrot_w4a4_forward: qweight_unpacked must be int8 [{N}, {K}]")
         x2d = x.reshape(-1, K).to(torch.float16).contiguous()
         a_q, a_s = ops.quant_pack_a_i4(x2d, ROT_GROUP)
-        out = ops.gemm_w4a4(a_q, a_s, qweight.contiguous(), wscales.reshape(N).float().contiguous(), bias)
+        ws = wscales.reshape(N).float().contiguous()
+        if qweight_unpacked is not None:
+            out = ops.gemm(a_q, a_s, qweight_unpacked.contiguous(), ws, bias)
+        else:
+            out = ops.gemm_w4a4(a_q, a_s, qweight.contiguous(), ws, bias)
         return out.reshape(x.shape[:-1] + (N,))
     return convrot_w4a4_forward
 

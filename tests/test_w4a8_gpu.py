@@ -129,10 +129,14 @@ def test_w4a4_convrot_forward_bit_exact(pkg, dev, M, N, K):
     ws = (g.random(N) * 1e-2 + 1e-4).astype(F32)
     bias = (g.standard_normal(N) * 0.01).astype(F16)
     fwd = pkg.int8_gemm.wrap_w4a4(None)
+    wide = pkg.ops.unpack_int4(dev_(packed, dev))  # the load-time int8 copy (qweight_unpacked)
     for b in (None, bias):
-        got = fwd(dev_(x, dev).view(1, M, K), dev_(packed, dev), dev_(ws, dev), None if b is None else dev_(b, dev), 256,
-                  torch.float16)
-        assert got.shape == (1, M, N)
         q_ref, s_ref = oq.quant_rows_i4(oq.rotate_rows(x, 256))
         ref = ogemm.epilogue(ogemm.int_mm(q_ref, ogemm.unpack_int4(packed)), s_ref, ws, b)
-        assert np.array_equal(got.cpu().numpy().reshape(M, N), ref)
+        for unpacked in (None, wide):
+            got = fwd(dev_(x, dev).view(1, M, K), dev_(packed, dev), dev_(ws, dev), None if b is None else dev_(b, dev),
+                      256, torch.float16, qweight_unpacked=unpacked)
+            assert got.shape == (1, M, N)
+            assert np.array_equal(got.cpu().numpy().reshape(M, N), ref)
+    with pytest.raises(NotImplementedError, match="qweight_unpacked"):
+        fwd(dev_(x, dev), dev_(packed, dev), dev_(ws, dev), None, 256, torch.float16, qweight_unpacked=wide[:, :-16])
