@@ -309,13 +309,18 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
             ss = 0.f;
             for (int w = 0; w < nwarps; ++w) ss += red[0][w];
             const uint64_t R2 = splat2(rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
-            const __half* srow = a.s + (int64_t)(row / a.L) * K;
-            const __half* trow = a.t + (int64_t)(row / a.L) * K;
+            // Without modulation rows (s = t = null) the result is the RMSNorm n itself.
+            const bool modulate = a.s != nullptr;
+            const __half* srow = modulate ? a.s + (int64_t)(row / a.L) * K : nullptr;
+            const __half* trow = modulate ? a.t + (int64_t)(row / a.L) * K : nullptr;
 #pragma unroll
             for (int o = 0; o < 4; ++o) {
                 const int k = k0 + 32 * o;
-                const uint4 sv = __ldg(reinterpret_cast<const uint4*>(srow + k));
-                const uint4 tv = __ldg(reinterpret_cast<const uint4*>(trow + k));
+                uint4 sv = make_uint4(0, 0, 0, 0), tv = make_uint4(0, 0, 0, 0);
+                if (modulate) {
+                    sv = __ldg(reinterpret_cast<const uint4*>(srow + k));
+                    tv = __ldg(reinterpret_cast<const uint4*>(trow + k));
+                }
                 const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.w + k));
                 const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.w + k) + 1);
                 const uint64_t W[4] = {pk2(w0.x, w0.y), pk2(w0.z, w0.w), pk2(w1.x, w1.y), pk2(w1.z, w1.w)};
@@ -326,7 +331,8 @@ __global__ void __launch_bounds__(512) prepass128_kernel(const PrepassArgs a) {
                     // n = fp16(x rstd (w + 1)); y = fp16(fp16(n s) + t) as exact fp16 pair operations (see
                     // prepass_kernel)
                     const uint32_t n = f2_to_h2(mul2(mul2(X[o][p], R2), add2(W[p], splat2(1.f))));
-                    y[o][p] = h2_as_u32(__hadd2_rn(__hmul2_rn(u32_as_h2(n), u32_as_h2(s2[p])), u32_as_h2(t2[p])));
+                    y[o][p] = modulate ? h2_as_u32(__hadd2_rn(__hmul2_rn(u32_as_h2(n), u32_as_h2(s2[p])), u32_as_h2(t2[p])))
+                                       : n;
                 }
             }
         } else {
@@ -534,8 +540,9 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
     }
 
     const __half* ur = two_inputs<ACT>() ? a.u + (int64_t)row * a.ldu : nullptr;
-    const __half* srow = ACT == ACT_MOD ? a.s + (int64_t)(row / a.L) * K : nullptr;
-    const __half* trow = ACT == ACT_MOD ? a.t + (int64_t)(row / a.L) * K : nullptr;
+    // Without modulation rows (s = t = null) the MOD flavour's result is the RMSNorm n itself.
+    const __half* srow = ACT == ACT_MOD && a.s ? a.s + (int64_t)(row / a.L) * K : nullptr;
+    const __half* trow = ACT == ACT_MOD && a.s ? a.t + (int64_t)(row / a.L) * K : nullptr;
 
     __half2 mx2 = __float2half2_rn(0.f);  // running max of |y| over this lane's values (fp16, exact)
     const int npass = (K + 511) >> 9;
@@ -570,13 +577,15 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
                 // n = fp16(x * rstd * (w + 1)) in fp32; then fp16(fp16(n * s) + t) as fp16 pairs: the product of two
                 // fp16 values is exact before its single rounding, and a sum of two fp16 values rounded once to
                 // fp16 equals the fp32 sum rounded to fp16, so the packed ops round exactly like the fp32 path.
-                uint4 xr[2], sr[2], tr[2];
+                uint4 xr[2], sr[2] = {}, tr[2] = {};
                 xr[0] = *reinterpret_cast<const uint4*>(rowbuf + k0);
                 xr[1] = *reinterpret_cast<const uint4*>(rowbuf + k0 + 8);
-                sr[0] = __ldg(reinterpret_cast<const uint4*>(srow + k0));
-                sr[1] = __ldg(reinterpret_cast<const uint4*>(srow + k0) + 1);
-                tr[0] = __ldg(reinterpret_cast<const uint4*>(trow + k0));
-                tr[1] = __ldg(reinterpret_cast<const uint4*>(trow + k0) + 1);
+                if (srow) {
+                    sr[0] = __ldg(reinterpret_cast<const uint4*>(srow + k0));
+                    sr[1] = __ldg(reinterpret_cast<const uint4*>(srow + k0) + 1);
+                    tr[0] = __ldg(reinterpret_cast<const uint4*>(trow + k0));
+                    tr[1] = __ldg(reinterpret_cast<const uint4*>(trow + k0) + 1);
+                }
                 const __half2* x2 = reinterpret_cast<const __half2*>(xr);
                 const __half2* s2 = reinterpret_cast<const __half2*>(sr);
                 const __half2* t2 = reinterpret_cast<const __half2*>(tr);
@@ -589,8 +598,8 @@ __global__ void __launch_bounds__(PP_WARPS * 32, 5) prepass_kernel(const Prepass
                                                          __fmul_rn(__fmul_rn(xa.y, rstd), __fadd_rn(w4.y, 1.f)));
                     const __half2 nb = __floats2half2_rn(__fmul_rn(__fmul_rn(xb.x, rstd), __fadd_rn(w4.z, 1.f)),
                                                          __fmul_rn(__fmul_rn(xb.y, rstd), __fadd_rn(w4.w, 1.f)));
-                    const float2 ya = __half22float2(__hadd2_rn(__hmul2_rn(na, s2[2 * i]), t2[2 * i]));
-                    const float2 yb = __half22float2(__hadd2_rn(__hmul2_rn(nb, s2[2 * i + 1]), t2[2 * i + 1]));
+                    const float2 ya = __half22float2(srow ? __hadd2_rn(__hmul2_rn(na, s2[2 * i]), t2[2 * i]) : na);
+                    const float2 yb = __half22float2(srow ? __hadd2_rn(__hmul2_rn(nb, s2[2 * i + 1]), t2[2 * i + 1]) : nb);
                     v[4 * i + 0] = ya.x;
                     v[4 * i + 1] = ya.y;
                     v[4 * i + 2] = yb.x;
@@ -875,9 +884,10 @@ extern "C" int b2_mod_quant_pack_a(const uint16_t* x, int64_t ldx, const float* 
     a.L = L;
     a.eps = eps;
     a.act_out = reinterpret_cast<__half*>(act_out);
-    if (!w || !s || !t || L <= 0) return fail(B2_ERR_INVALID, "mod: null weight/scale/shift or L <= 0");
-    if (!aligned16(w) || !aligned16(s) || !aligned16(t))
+    if (!w || !s != !t || (s && L <= 0)) return fail(B2_ERR_INVALID, "mod: null weight, one of scale/shift null, or L <= 0");
+    if (!aligned16(w) || (s && (!aligned16(s) || !aligned16(t))))
         return fail(B2_ERR_UNSUPPORTED, "mod: w, s, t must be 16-byte aligned");
+    if (!s) a.L = 1;
     if (int rc = validate(a, rot_group)) return rc;
     if (M == 0) return B2_OK;
     return launch_rot<ACT_MOD>(a, rot_group, (cudaStream_t)stream);

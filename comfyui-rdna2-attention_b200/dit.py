@@ -194,7 +194,6 @@ class DiTStack:
         # Buffers are allocated once and reused by every block and step (graph-capturable).
         dev = device
         self.ones = torch.ones((b, D), dtype=torch.float16, device=dev)
-        self.zeros = torch.zeros((b, D), dtype=torch.float16, device=dev)
         self.q8 = torch.empty((M * max(D, F),), dtype=torch.int8, device=dev)
         self.sa = torch.empty((M,), dtype=torch.float32, device=dev)
         self.qkv = torch.empty((M, 3 * hl * cfg.head_dim), dtype=torch.float16, device=dev)
@@ -213,7 +212,7 @@ class DiTStack:
         M = b * T
         q8 = self.q8[:M * D].view(M, D)
         with t("prepass"):
-            ops.mod_quant_pack_a(x.view(M, D), blk.norm1, self.ones, self.zeros, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
+            ops.mod_quant_pack_a(x.view(M, D), blk.norm1, None, None, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
         if self.probe:
             self.probe("norm1", x.view(M, D), q8, self.sa)
         with t("gemm", 2 * M * D * self.qkv.shape[1]):
@@ -251,7 +250,7 @@ class DiTStack:
         if self.probe:
             self.probe("out_proj", self.xa)
         with t("prepass"):
-            ops.mod_quant_pack_a(self.xa, blk.norm2, self.ones, self.zeros, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
+            ops.mod_quant_pack_a(self.xa, blk.norm2, None, None, T, cfg.eps, cfg.rot_group, out=(q8, self.sa))
         if self.probe:
             self.probe("norm2", q8, self.sa)
         with t("gemm", 2 * M * D * 2 * F):

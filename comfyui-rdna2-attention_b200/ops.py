@@ -128,13 +128,16 @@ def situ_quant_pack_a(x, rot_group=ROT_NONE, act_out=None, out=None):
 
 def mod_quant_pack_a(x, weight, s_rows, t_rows, L, eps, rot_group=ROT_NONE, act_out=None, out=None):
     """int8 of the modulated RMSNorm fp16(fp16(fp16(x*rstd*(w+1)) * s) + t) after an optional rotation.
-    x fp16 [M, K]; weight fp32 [K]; s_rows (= 1 + scale), t_rows fp16 [M // L, K]."""
+    x fp16 [M, K]; weight fp32 [K]; s_rows (= 1 + scale), t_rows fp16 [M // L, K]; both None: the RMSNorm alone
+    (the same int8 as s = 1, t = 0)."""
     _half2d(x, "x")
     M, K = x.shape
     if L < 1:
         _fail(f"L={L} must be at least 1")
+    if (s_rows is None) != (t_rows is None):
+        _fail("modulation scale and shift are both given or both None")
     for t, n in ((s_rows, "scale"), (t_rows, "shift")):
-        if t.dtype != torch.float16 or not t.is_contiguous() or t.numel() < ((M + L - 1) // L) * K:
+        if t is not None and (t.dtype != torch.float16 or not t.is_contiguous() or t.numel() < ((M + L - 1) // L) * K):
             _fail(f"modulation {n} must be contiguous fp16 [M / L, K]")
     if weight.dtype != torch.float32 or not weight.is_contiguous() or weight.numel() != K:
         _fail("norm weight must be contiguous fp32 [K]")

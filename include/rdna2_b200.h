@@ -83,7 +83,8 @@ int b2_gate_quant_pack_a(const uint16_t* x, const uint16_t* gate, int64_t ld, in
 int b2_situ_quant_pack_a(const uint16_t* x, int64_t ldx, int8_t* q, float* scale, int M, int K, int rot_group,
                          uint16_t* act_out, void* stream);
 /* h = fp16(fp16(fp16(x * rstd * (w + 1)) * s) + t), rstd = rsqrt(mean(x^2) + eps); s (= 1 + scale)
- * and t are fp16 [M / L, K] rows (int8_gemm.hip:139-143,167-191; caller int8_gemm.py:176-186). */
+ * and t are fp16 [M / L, K] rows (int8_gemm.hip:139-143,167-191; caller int8_gemm.py:176-186). With s and t both
+ * null there is no modulation: h = fp16(x * rstd * (w + 1)), the same int8 as s = 1, t = 0 without reading them. */
 int b2_mod_quant_pack_a(const uint16_t* x, int64_t ldx, const float* w, const uint16_t* s, const uint16_t* t, int L,
                         float eps, int8_t* q, float* scale, int M, int K, int rot_group, uint16_t* act_out,
                         void* stream);

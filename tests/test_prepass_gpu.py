@@ -136,6 +136,29 @@ def test_mod_prepass(pkg, dev, rot):
 
 
 @pytest.mark.parametrize("rot", [0, 128, 256])
+@pytest.mark.parametrize("M,K", [(300, 3072), (33, 640)])
+def test_mod_prepass_without_modulation(pkg, dev, rot, M, K):
+    """The RMSNorm alone (scale and shift None, as the configuration-4 block uses it): the same int8 and scales, bit
+    for bit, and the same activation, as modulation rows of ones and zeros; through the one-row-per-CTA kernel
+    (K = 3072 under the block-128 rotation) and the warp-per-row kernel (the other cases)."""
+    if rot and K % rot:
+        pytest.skip("K not a multiple of the rotation group")
+    g = np.random.default_rng(M + K + rot)
+    x = (g.standard_normal((M, K)) * 2).astype(F16)
+    x[3, :8] = 0  # zero activations: +0 and -0 must quantize alike
+    w = (g.standard_normal(K) * 0.1).astype(np.float32)
+    ones, zeros = torch.ones((1, K), dtype=torch.float16, device=dev), torch.zeros((1, K), dtype=torch.float16, device=dev)
+    act_a = torch.empty((M, K), dtype=torch.float16, device=dev)
+    act_b = torch.empty((M, K), dtype=torch.float16, device=dev)
+    qa, sa = pkg.ops.mod_quant_pack_a(dev_(x, dev), dev_(w, dev), ones, zeros, M, 1e-6, rot, act_out=act_a)
+    qb, sb = pkg.ops.mod_quant_pack_a(dev_(x, dev), dev_(w, dev), None, None, M, 1e-6, rot, act_out=act_b)
+    assert torch.equal(qa, qb) and torch.equal(sa, sb)
+    assert torch.equal(act_a, act_b)
+    with pytest.raises(RuntimeError, match="both given or both None"):
+        pkg.ops.mod_quant_pack_a(dev_(x, dev), dev_(w, dev), ones, None, M, 1e-6, rot)
+
+
+@pytest.mark.parametrize("rot", [0, 128, 256])
 @pytest.mark.parametrize("M,K", [(97, 3072), (33, 640)])
 def test_situ_prepass(pkg, dev, rot, M, K):
     """situ on [hidden | gate] rows (int8_gemm.hip:118-127): the fp16 activation within two steps of the float32
