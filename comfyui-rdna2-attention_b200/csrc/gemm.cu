@@ -154,7 +154,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
     const uint64_t sa2 = splat2(sa);
     const int nc = min(NB, (g.N - n0 + 15) / 16);
     const bool res = g.R != nullptr;
-    const __half* gate_row = (res && row_ok) ? g.G + (int64_t)(m / g.L) * g.N : nullptr;
+    const __half* gate_row = (res && row_ok && g.G) ? g.G + (int64_t)(m / g.L) * g.N : nullptr;  // G null: gate 1
     const int sw = (lane >> 2) & 1;
     bool ok = true;
     EpiParams P[2];
@@ -213,7 +213,9 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, const CUtensorM
                     v = pk2(__fadd_rn(f.x, bv[2 * q]), __fadd_rn(f.y, bv[2 * q + 1]));
                 }
                 uint32_t y = f2_to_h2(v);
-                if (res) y = h2_as_u32(__hadd2_rn(u32_as_h2(rw[q]), __hmul2_rn(u32_as_h2(gw[q]), u32_as_h2(y))));
+                if (res)  // with no gate, fp16(1 * y) = y: the same bits without the gate rows
+                    y = h2_as_u32(g.G ? __hadd2_rn(u32_as_h2(rw[q]), __hmul2_rn(u32_as_h2(gw[q]), u32_as_h2(y)))
+                                      : __hadd2_rn(u32_as_h2(rw[q]), u32_as_h2(y)));
                 ow[q] = y;
             }
             *slot = o;
@@ -771,8 +773,8 @@ using namespace b2;
 extern "C" int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const float* ws, const uint16_t* bias,
                        uint16_t* C, int M, int N, int K, const uint16_t* R, const uint16_t* G, int L, void* stream) {
     if (!as || !ws || !C) return fail(B2_ERR_INVALID, "gemm: null scale or output");
-    if (R && (!G || L <= 0)) return fail(B2_ERR_INVALID, "gemm: residual needs a gate and L > 0");
-    if (!aligned16(C) || !aligned16(ws) || (bias && !aligned16(bias)) || (R && (!aligned16(R) || !aligned16(G))))
+    if (G && (!R || L <= 0)) return fail(B2_ERR_INVALID, "gemm: a gate needs a residual and L > 0");
+    if (!aligned16(C) || !aligned16(ws) || (bias && !aligned16(bias)) || (R && !aligned16(R)) || (G && !aligned16(G)))
         return fail(B2_ERR_UNSUPPORTED, "gemm: C, ws, bias, R, G must be 16-byte aligned");
     GemmArgs g{};
     g.as = as;

@@ -193,7 +193,6 @@ class DiTStack:
         self.hl = hl
         # Buffers are allocated once and reused by every block and step (graph-capturable).
         dev = device
-        self.ones = torch.ones((b, D), dtype=torch.float16, device=dev)
         self.q8 = torch.empty((M * max(D, F),), dtype=torch.int8, device=dev)
         self.sa = torch.empty((M,), dtype=torch.float32, device=dev)
         self.qkv = torch.empty((M, 3 * hl * cfg.head_dim), dtype=torch.float16, device=dev)
@@ -246,7 +245,7 @@ class DiTStack:
         if self.probe:
             self.probe("out_prepass", q8, self.sa)
         with t("gemm", 2 * M * D * D):
-            ops.gemm(q8, self.sa, blk.w_o, blk.s_o, residual=x2, gate=self.ones, L=T, out=self.xa)
+            ops.gemm(q8, self.sa, blk.w_o, blk.s_o, residual=x2, out=self.xa)
         if self.probe:
             self.probe("out_proj", self.xa)
         with t("prepass"):
@@ -263,7 +262,7 @@ class DiTStack:
         if self.probe:
             self.probe("down_prepass", q8f, self.sa)
         with t("gemm", 2 * M * F * D):
-            ops.gemm(q8f, self.sa, blk.w_down, blk.s_down, residual=self.xa, gate=self.ones, L=T, out=x2)
+            ops.gemm(q8f, self.sa, blk.w_down, blk.s_down, residual=self.xa, out=x2)
         if self.probe:
             self.probe("down", x2)
         return x

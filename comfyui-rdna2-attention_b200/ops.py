@@ -174,14 +174,15 @@ def _gemm_operands(a_q, a_scale, w_q, w_scale, name):
 
 
 def gemm(a_q, a_scale, w_q, w_scale, bias=None, residual=None, gate=None, L=1, out=None):
-    """fp16 [M, N] = (a_q . w_q^T) * a_scale[m] * w_scale[n] (+ bias) (, residual + gate * y)."""
+    """fp16 [M, N] = (a_q . w_q^T) * a_scale[m] * w_scale[n] (+ bias) (, residual + gate * y; without a gate,
+    residual + y)."""
     M, N, K = _gemm_operands(a_q, a_scale, w_q, w_scale, "gemm")
     _vec(bias, N, torch.float16, "gemm bias")
+    if gate is not None and residual is None:
+        _fail("a gate needs a residual")
     if residual is not None:
-        if gate is None:
-            gate = torch.ones((1, N), dtype=torch.float16, device=a_q.device)
-            L = max(M, 1)
         _exact(residual, (M, N), torch.float16, "residual")
+    if gate is not None:
         if gate.dtype != torch.float16 or not gate.is_contiguous() or gate.shape[-1] != N:
             _fail("gate must be contiguous fp16 [M / L, N]")
         if L < 1 or gate.numel() // N < (M + L - 1) // L:

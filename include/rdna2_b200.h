@@ -94,6 +94,7 @@ int b2_mod_quant_pack_a(const uint16_t* x, int64_t ldx, const float* w, const ui
  * per-call pack_b (:271), launched from int8_gemm.py:70-79. B is the weight as stored, int8 [N, K].
  *   y = (float)acc * as[m] * ws[n] (+ bias[n])  -> fp16                     (int8_gemm.hip:382-383)
  *   with R: out = fp16(R[m,n] + fp16(G[m / L, n] * y))                      (int8_gemm.hip:394-400)
+ *   with R and G null: out = fp16(R[m,n] + y), the same as a gate of ones (no gate rows read)
  * Needs K % 16 == 0, N % 8 == 0, 16-byte aligned A and B.
  * ------------------------------------------------------------------------------------------------ */
 int b2_gemm(const int8_t* A, const int8_t* B, const float* as, const float* ws, const uint16_t* bias, uint16_t* C,

@@ -72,6 +72,10 @@ def test_residual_epilogue_bit_exact(pkg, dev, B, L, N, K):
     got = pkg.ops.gemm(dev_(a, dev), dev_(sa, dev), dev_(b, dev), dev_(sw, dev), residual=dev_(R, dev), gate=dev_(G, dev), L=L)
     ref = ogemm.epilogue(ogemm.int_mm(a, b), sa, sw, R=R, G=G, L=L)
     assert np.array_equal(got.cpu().numpy(), ref)
+    # No gate: R + y, bit for bit the gate of ones (fp16(1 * y) = y), through the 1-CTA (M = 300) and pair kernels.
+    ones = np.ones((1, N), F16)
+    got1 = pkg.ops.gemm(dev_(a, dev), dev_(sa, dev), dev_(b, dev), dev_(sw, dev), residual=dev_(R, dev))
+    assert np.array_equal(got1.cpu().numpy(), ogemm.epilogue(ogemm.int_mm(a, b), sa, sw, R=R, G=ones, L=M))
 
 
 @pytest.mark.parametrize("rot", [128, 256])
